@@ -1,0 +1,409 @@
+"""Benchmark of the B200 MXFP4/INT8 MoE layer (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (N=1): the decode MoE layer of BASELINE configs[2]
+(H=7168, I=2048, 256 experts, top-8 sigmoid+bias routing, M=64 tokens),
+weights random MXFP4 (uniform codes, UE8M0 exponents uniform in [-8,-4])
+repacked on the GPU.  A second object reports the prefill layer
+(configs[3], M=8192 with Zipf(1.1)-skewed routing).  One step = one full
+layer forward (align, quant, W13+SwiGLU GEMM, quant, W2 GEMM, combine).
+Inputs larger than L2 (5.7 GB of weights) are streamed every step, so L2 is
+not flushed.
+
+``--impl reference`` times the reference's CPU torch MoE (restated in
+oracle/, the reference being Python that does not travel) on the host cores
+on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (str(ROOT), str(ROOT / "deepseek-v4-a100-sglang_b200"), str(ROOT / "tests")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+H, I, E, TOPK = 7168, 2048, 256, 8
+DECODE_M, PREFILL_M = 64, 8192
+EXP_RANGE = (-8, -4)
+
+
+def peaks():
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"dsv4_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        try:
+            self.path.unlink()
+        except Exception:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_weights(dev, seed):
+    """Random MXFP4 expert weights generated on the GPU, repacked there."""
+    import torch
+    import dsv4_b200 as D
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    out = []
+    for n, k in ((2 * I, H), (H, I)):
+        w = torch.randint(0, 256, (E, n, k // 2), device=dev, dtype=torch.uint8, generator=g)
+        s = torch.randint(127 + EXP_RANGE[0], 127 + EXP_RANGE[1] + 1, (E, n, k // 32), device=dev,
+                          dtype=torch.uint8, generator=g)
+        out.extend(D.remap_mxfp4_weight_for_int8(w, s))
+        del w, s
+    torch.cuda.synchronize()
+    return D.Mxfp4Int8MoeWeights(*out, 3)
+
+
+def weight_bytes_per_expert():
+    kb13, kb2 = H // 32, I // 32
+    w13 = 2 * I * H // 2 + (kb13 + 3) // 4 * 2 * I + 4 * 2 * I
+    w2 = H * I // 2 + (kb2 + 3) // 4 * H + 4 * H
+    return w13, w2
+
+
+class Layer:
+    """The forward of mxfp4_int8_moe_forward, step by step through the public
+    op API, with CUDA events around the two GEMM launches."""
+
+    def __init__(self, weights, m, dev):
+        import torch
+        import dsv4_b200 as D
+        self.D, self.w, self.m, self.dev = D, weights, m, dev
+        self.bm, self.bn = D.select_mxfp4_int8_moe_tile_shape(m, TOPK, E)
+        self.inter = torch.empty((m * TOPK, I), device=dev, dtype=torch.bfloat16)
+        self.routed = torch.empty((m * TOPK, H), device=dev, dtype=torch.bfloat16)
+        self.out = torch.empty((m, H), device=dev, dtype=torch.bfloat16)
+        self.ev = []
+
+    def __call__(self, x, ids, tw, record=False):
+        import torch
+        import dsv4_b200.jit_ops as J
+        D, w, m = self.D, self.w, self.m
+        s, e, n = D.moe_align_block_size(ids, self.bm, E)
+        q, qs = D.quantize_per_token_int8(x)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if record:
+            evs[0].record()
+        J.mxfp4_int8_moe_gemm_swiglu(q, qs, w.w13_mxfp4, w.w13_shift2, w.w13_channel_scale,
+                                     self.inter, s, e, n, hidden_size=H, intermediate_size=I,
+                                     topk=TOPK, block_m=self.bm, num_valid_tokens=m * TOPK)
+        if record:
+            evs[1].record()
+        q2, qs2 = D.quantize_per_token_int8(self.inter)
+        if record:
+            evs[2].record()
+        J.mxfp4_int8_moe_gemm(q2, qs2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale, self.out, tw,
+                              s, e, n, hidden_size=H, intermediate_size=I, topk=TOPK,
+                              block_m=self.bm, block_n=self.bn, source_rows_are_slots=True,
+                              num_valid_tokens=m * TOPK, routed_out=self.routed)
+        if record:
+            evs[3].record()
+            self.ev.append(evs)
+        J.mxfp4_int8_moe_reduce(self.routed, tw, self.out, hidden_size=H, intermediate_size=I,
+                                topk=TOPK, block_m=self.bm, num_valid_tokens=m * TOPK)
+        return self.out
+
+    def gemm_ms(self):
+        w13 = [a.elapsed_time(b) for a, b, _, _ in self.ev]
+        w2 = [c.elapsed_time(d) for _, _, c, d in self.ev]
+        return statistics.mean(w13), statistics.mean(w2)
+
+
+LAUNCHES_PER_STEP = 6  # align, quant, W13+SwiGLU, quant, W2, combine
+
+
+def routing(m, seed, zipf):
+    import gen_inputs as G
+    return G.routing_sigmoid_bias_topk(m, E, TOPK, seed, zipf_s=zipf)
+
+
+def run_workload(weights, m, zipf, steps, warmup, dev, rank, world, hbm, tops_i8, sample_clocks):
+    import torch
+    import torch.distributed as dist
+    ids, tw = routing(m, 1000 + rank, zipf)
+    import gen_inputs as G
+    x = G.randn_bf16((m, H), 2000 + rank)
+    xd, idd, twd = x.to(dev), ids.to(dev), tw.to(dev)
+    layer = Layer(weights, m, dev)
+    for _ in range(warmup):
+        layer(xd, idd, twd)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = Clocks(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                 int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[torch.cuda.current_device()]))
+    with (clk if sample_clocks else _Null()):
+        start.record()
+        for _ in range(steps):
+            layer(xd, idd, twd, record=True)
+        stop.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    w13_ms, w2_ms = layer.gemm_ms()
+    touched = int(torch.unique(ids).numel())
+    b13, b2 = weight_bytes_per_expert()
+    act13 = m * H + 4 * m + m * TOPK * I * 2
+    act2 = m * TOPK * I + 4 * m * TOPK + m * TOPK * H * 2
+    res = {"ms": ms, "w13_ms": w13_ms, "w2_ms": w2_ms, "touched": touched,
+           "w13_bytes": touched * b13 + act13, "w2_bytes": touched * b2 + act2,
+           "layer_bytes": touched * (b13 + b2) + m * H * 4 + m * TOPK * 8,
+           "w13_ops": 2 * m * TOPK * H * 2 * I, "w2_ops": 2 * m * TOPK * I * H,
+           "clocks": clk.summary() if sample_clocks else None, "bm": layer.bm}
+    # end to end: pinned host inputs in, host output back, every step
+    hx, hid, htw = x.pin_memory(), ids.pin_memory(), tw.pin_memory()
+    hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
+    import dsv4_b200 as D
+    for _ in range(2):
+        o = D.mxfp4_int8_moe_forward(hx.to(dev, non_blocking=True), weights,
+                                     hid.to(dev, non_blocking=True), htw.to(dev, non_blocking=True),
+                                     hidden_size=H, intermediate_size=I)
+        hout.copy_(o, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        o = D.mxfp4_int8_moe_forward(hx.to(dev, non_blocking=True), weights,
+                                     hid.to(dev, non_blocking=True), htw.to(dev, non_blocking=True),
+                                     hidden_size=H, intermediate_size=I)
+        hout.copy_(o, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    res["e2e_ms"] = e2e_ms
+    res["h2d"] = m * H * 2 + m * TOPK * 4 * 2
+    res["d2h"] = m * H * 2
+    return res
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def cpu_reference_sample(steps, warmup, tokens_per_step=1):
+    """The reference's CPU torch MoE (oracle restatement of
+    tests/test_mxfp4_int8_moe.py:51-79) on a bounded sample of the decode
+    workload: per step `tokens_per_step` tokens with all of their top-8 routes,
+    dequantising the experts they touch (as the reference does) then fp32
+    matmuls.  Returns tokens/s and the thread count."""
+    import torch
+    import gen_inputs as G
+    from oracle import mxfp4_int8_oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ids, tw = routing(DECODE_M, 1000, None)
+    x = G.randn_bf16((DECODE_M, H), 2000)
+    times = []
+    for step in range(warmup + steps):
+        t0 = step % DECODE_M
+        sl = slice(t0, t0 + tokens_per_step)
+        sub_ids = ids[sl]
+        experts = torch.unique(sub_ids).tolist()
+        remap = {e: j for j, e in enumerate(experts)}
+        local_ids = sub_ids.clone().apply_(lambda v: remap[v])
+        w13, s13 = G.make_random_packed_mxfp4(len(experts), 2 * I, H, 7 + step, exp_range=EXP_RANGE)
+        w2, s2 = G.make_random_packed_mxfp4(len(experts), H, I, 8 + step, exp_range=EXP_RANGE)
+        t = time.perf_counter()
+        O.mxfp4_moe_reference_torch(x[sl], w13, s13, w2, s2, local_ids, tw[sl])
+        dt = time.perf_counter() - t
+        if step >= warmup:
+            times.append(dt)
+    sec = statistics.median(times)
+    return tokens_per_step / sec, threads, sec
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = min(args.steps, 10)
+        tps, threads, sec = cpu_reference_sample(steps, min(args.warmup, 1))
+        line = {"metric": "MoE layer tokens/s (decode M=64)", "value": tps, "unit": "tokens/s",
+                "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": min(args.warmup, 1),
+                "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "decode MoE layer H=7168 I=2048 E=256 top-8 M=64",
+                           "sample": "1 token/step, its 8 routes"},
+                "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                 "sample": "1 token of the M=64 decode batch per step: dequantise its 8 "
+                                           "experts (fp32) + per-route SwiGLU MLP, reference torch CPU MoE"},
+                "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl")
+    dev = torch.device("cuda", local if world > 1 else torch.cuda.current_device())
+    import dsv4_b200 as D  # noqa: F401
+    hbm, bf16_tf, peak_src = peaks()
+    tops_i8 = 2.0 * bf16_tf
+
+    weights = make_weights(dev, 42)
+    dec = run_workload(weights, DECODE_M, None, args.steps, args.warmup, dev, rank, world, hbm,
+                       tops_i8, sample_clocks=True)
+    pre = None
+    if not args.no_prefill:
+        pre = run_workload(weights, PREFILL_M, 1.1, max(3, args.steps // 4), args.warmup, dev,
+                           rank, world, hbm, tops_i8, sample_clocks=False)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        tps, threads, sec = cpu_reference_sample(3, 1)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": "1 token of the M=64 decode batch per step (3 steps, median): dequantise its 8 "
+                         "experts to fp32 + per-route SwiGLU MLP, the reference's torch CPU MoE restated"}
+    if rank != 0:
+        dist.barrier() if world > 1 else None
+        return
+
+    total_tokens = DECODE_M * world
+    w13_gbs = dec["w13_bytes"] / (dec["w13_ms"] * 1e-3) / 1e9
+    line = {
+        "metric": "MoE layer tokens/s (decode M=64)",
+        "value": total_tokens / (dec["ms"] * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dec["ms"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 x mxfp4 -> int32 (bf16 I/O)",
+        "data": "synthetic",
+        "config": {"workload": "decode MoE layer (BASELINE configs[2]): H=7168 I=2048 E=256 top-8 "
+                               "sigmoid+bias routing, M=64 tokens/GPU, MXFP4 weights exps U[-8,-4]",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "block_m": dec["bm"], "l2": "not flushed: 5.7 GB of weights streamed per step",
+                   "experts_touched": dec["touched"]},
+        "roofline": {"bound": "hbm", "kernel": "W13 grouped GEMM + fused SwiGLU",
+                     "achieved": w13_gbs, "peak": hbm, "unit": "GB/s", "frac": w13_gbs / hbm,
+                     "traffic": None, "peak_source": peak_src,
+                     "algorithmic_bytes_per_launch": dec["w13_bytes"],
+                     "launch_ms": dec["w13_ms"]},
+        "layer_roofline": {"bound": "hbm", "bytes_per_step": dec["layer_bytes"],
+                           "achieved": dec["layer_bytes"] / (dec["ms"] * 1e-3) / 1e9,
+                           "frac": dec["layer_bytes"] / (dec["ms"] * 1e-3) / 1e9 / hbm,
+                           "w2_gemm_ms": dec["w2_ms"],
+                           "w2_gbs": dec["w2_bytes"] / (dec["w2_ms"] * 1e-3) / 1e9},
+        "e2e": {"value": total_tokens / (dec["e2e_ms"] * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"],
+                "ms_per_step": dec["e2e_ms"]},
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "clocks": dec["clocks"],
+    }
+    if pre is not None:
+        ops = pre["w13_ops"] + pre["w2_ops"]
+        line["prefill"] = {
+            "workload": "prefill MoE layer (BASELINE configs[3]): M=8192, Zipf(1.1) expert skew",
+            "value": PREFILL_M * world / (pre["ms"] * 1e-3), "unit": "tokens/s",
+            "ms_per_step": pre["ms"], "block_m": pre["bm"],
+            "roofline": {"bound": "tensor", "achieved": ops / (pre["ms"] * 1e-3) / 1e12,
+                         "peak": tops_i8, "unit": "TOP/s (int8)",
+                         "frac": ops / (pre["ms"] * 1e-3) / 1e12 / tops_i8,
+                         "peak_source": f"2 x {peak_src} bf16 dense (kind::i8 rate = 2x kind::f16)",
+                         "w13_tops": pre["w13_ops"] / (pre["w13_ms"] * 1e-3) / 1e12,
+                         "w2_tops": pre["w2_ops"] / (pre["w2_ms"] * 1e-3) / 1e12},
+            "e2e": {"value": PREFILL_M * world / (pre["e2e_ms"] * 1e-3), "unit": "tokens/s"},
+        }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

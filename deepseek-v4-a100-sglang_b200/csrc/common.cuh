@@ -1,0 +1,275 @@
+// Shared device helpers for the B200 (sm_100a) MXFP4/INT8 MoE kernels:
+// status reporting, bounded mbarrier waits, bulk async copies, tcgen05
+// (TMEM alloc / MMA / commit / load) and the MXFP4 -> INT8 nibble decode.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "dsv4_b200.h"
+
+namespace dsv4 {
+
+// ---------------------------------------------------------------------------
+// Device-side status word.  A kernel that gives up on a wait records a code
+// here (first writer wins) and runs to completion with garbage output instead
+// of hanging the GPU; the host reads it with dsv4_b200_get_device_status().
+// ---------------------------------------------------------------------------
+// Defined here: the library is a single translation unit (dsv4_b200.cu).
+__device__ int g_device_status = 0;
+
+enum DeviceErr : int {
+  kErrNone = 0,
+  kErrWaitPackedFull = 0x101,
+  kErrWaitAbEmpty = 0x102,
+  kErrWaitAbFull = 0x103,
+  kErrWaitAccFull = 0x104,
+  kErrWaitPackedEmpty = 0x105,
+};
+
+// Wait budget: ~2 s of %globaltimer per wait.
+constexpr unsigned long long kWaitBudgetNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void record_error(int code) {
+  atomicCAS(&g_device_status, 0, code);
+}
+
+__device__ __forceinline__ bool device_error_pending() {
+  return *reinterpret_cast<volatile int*>(&g_device_status) != 0;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and records `code`) when the budget runs out
+// or another wait in the grid already failed.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  unsigned long long t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++n & 255u) == 0) {
+      if (device_error_pending()) return false;
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        record_error(code);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Bulk async copies (TMA engine, untiled) and Ampere-style cp.async
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// global -> shared bulk copy; dst/src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Make generic-proxy shared-memory writes visible to the async proxy
+// (tcgen05.mma operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (5th-gen tensor core, TMEM accumulators)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once all tcgen05.mma issued so far by this thread complete.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 32 bits, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, int32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row atoms of
+// 8 x 128 B stacked every 1024 B (stride byte offset), version 1, layout
+// SWIZZLE_128B (2).  Start address must be 1024-aligned apart from the
+// in-row K offset (0/32/64/96 B), which the hardware folds into the swizzle.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);   // start address
+  d |= static_cast<uint64_t>(1u) << 16;                   // LBO (unused for SW128 K-major)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;           // SBO = 1024 B
+  d |= static_cast<uint64_t>(1u) << 46;                   // descriptor version (sm100)
+  d |= static_cast<uint64_t>(2u) << 61;                   // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::i8: s8 x s8 -> s32, both K-major.
+__device__ __forceinline__ uint32_t idesc_i8(uint32_t m, uint32_t n) {
+  return (2u << 4)            // D format S32
+         | (1u << 7)          // A signed int8
+         | (1u << 10)         // B signed int8
+         | ((n >> 3) << 17)   // N / 8
+         | ((m >> 4) << 24);  // M / 16
+}
+
+// ---------------------------------------------------------------------------
+// MXFP4 -> INT8 decode.
+// Code nibble c: magnitude index c & 7 into {0,1,2,3,4,6,8,12}, sign c & 8,
+// value = +/- (mag << shift), shift in [0,3] (max 96, fits int8).
+// prmt with a raw nibble selector copies byte (c & 7) of {t1,t0} when c < 8
+// and replicates its sign bit (0, the table bytes are positive) when c >= 8:
+// that yields the positive part P.  Flipping every nibble's bit 3 yields the
+// negative part N.  P and N are disjoint per byte, so P - N = P | (-N) with a
+// borrow-free per-byte negate (N <= 0x60).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t neg_bytes_or(uint32_t p, uint32_t n) {
+  // p | ((0x80808080 - n) ^ 0x80808080)
+  return p | ((0x80808080u - n) ^ 0x80808080u);
+}
+
+// Decode the 8 nibbles of `q` (low nibble first) into 8 int8:
+// lo <- nibbles 0..3, hi <- nibbles 4..7.
+__device__ __forceinline__ void decode8(uint32_t q, uint32_t t0, uint32_t t1, uint32_t& lo,
+                                        uint32_t& hi) {
+  const uint32_t qn = q ^ 0x88888888u;
+  const uint32_t p_lo = prmt(t0, t1, q);
+  const uint32_t n_lo = prmt(t0, t1, qn);
+  const uint32_t p_hi = prmt(t0, t1, q >> 16);
+  const uint32_t n_hi = prmt(t0, t1, qn >> 16);
+  lo = neg_bytes_or(p_lo, n_lo);
+  hi = neg_bytes_or(p_hi, n_hi);
+}
+
+__device__ __forceinline__ void decode_tables(uint32_t shift, uint32_t& t0, uint32_t& t1) {
+  t0 = 0x03020100u << shift;
+  t1 = 0x0C080604u << shift;
+}
+
+}  // namespace dsv4

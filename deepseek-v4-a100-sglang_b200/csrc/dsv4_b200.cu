@@ -1,0 +1,473 @@
+// C ABI of the B200 MXFP4/INT8 MoE path (declared in include/dsv4_b200.h).
+// Single translation unit: the device status word and every kernel live here.
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "small_kernels.cuh"
+
+namespace dsv4 {
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return DSV4_OK;
+}
+
+#define DSV4_REQUIRE(cond, ...) \
+  do {                          \
+    if (!(cond)) return fail(DSV4_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+constexpr int kMaxDevices = 64;
+std::mutex g_init_mu;
+bool g_inited[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
+
+template <int TN, int EPI>
+struct GemmKernel {
+  static constexpr int kDW = TN <= 64 ? 4 : 8;
+  static constexpr int kThreads = (4 + kDW) * 32;
+  static constexpr int kSmem = TcGemmCfg<TN>::kSmemLaunch;
+  static void* fn() { return reinterpret_cast<void*>(&mxfp4_int8_tc_gemm_kernel<TN, EPI, kDW>); }
+};
+
+template <int EPI>
+cudaError_t set_attrs_epi() {
+  cudaError_t e = cudaSuccess;
+  auto one = [&](void* f, int smem) {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  };
+  one(GemmKernel<16, EPI>::fn(), GemmKernel<16, EPI>::kSmem);
+  one(GemmKernel<32, EPI>::fn(), GemmKernel<32, EPI>::kSmem);
+  one(GemmKernel<64, EPI>::fn(), GemmKernel<64, EPI>::kSmem);
+  one(GemmKernel<128, EPI>::fn(), GemmKernel<128, EPI>::kSmem);
+  one(GemmKernel<256, EPI>::fn(), GemmKernel<256, EPI>::kSmem);
+  return e;
+}
+
+constexpr int kAlignMaxExperts = 1024;
+int align_smem_bytes(int experts) { return (32 * experts + experts + 1 + 32) * 4; }
+
+int ensure_init() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(DSV4_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (g_inited[dev]) return DSV4_OK;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0)
+    return fail(DSV4_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                dev, major, minor);
+  e = set_attrs_epi<kEpiBf16>();
+  if (e == cudaSuccess) e = set_attrs_epi<kEpiI32>();
+  if (e == cudaSuccess) e = set_attrs_epi<kEpiSwiglu>();
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(reinterpret_cast<void*>(&moe_align_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             align_smem_bytes(kAlignMaxExperts));
+  if (e != cudaSuccess)
+    return fail(DSV4_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  cudaDeviceGetAttribute(&g_sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+  g_inited[dev] = true;
+  return DSV4_OK;
+}
+
+int sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
+}
+
+template <int EPI>
+int launch_gemm(int tn, dim3 grid, const TcGemmParams& p, cudaStream_t st) {
+  switch (tn) {
+#define DSV4_CASE(T)                                                                     \
+  case T:                                                                                \
+    mxfp4_int8_tc_gemm_kernel<T, EPI, GemmKernel<T, EPI>::kDW>                           \
+        <<<grid, GemmKernel<T, EPI>::kThreads, GemmKernel<T, EPI>::kSmem, st>>>(p);      \
+    break;
+    DSV4_CASE(16)
+    DSV4_CASE(32)
+    DSV4_CASE(64)
+    DSV4_CASE(128)
+    DSV4_CASE(256)
+#undef DSV4_CASE
+    default:
+      return fail(DSV4_ERR_INVALID_ARGUMENT, "unsupported token tile %d", tn);
+  }
+  return check_launch("mxfp4_int8_tc_gemm_kernel");
+}
+
+int64_t align_capacity(int64_t numel, int64_t experts, int64_t bm) {
+  return numel < experts + 1 ? numel * bm : numel + (experts + 1) * (bm - 1);
+}
+
+int check_weights(int64_t experts, int64_t n, int64_t k, int64_t shift_stride) {
+  DSV4_REQUIRE(experts >= 1, "num_experts must be >= 1, got %lld", (long long)experts);
+  DSV4_REQUIRE(n > 0 && n % 128 == 0, "N must be a positive multiple of 128, got %lld",
+               (long long)n);
+  DSV4_REQUIRE(k > 0 && k % 128 == 0, "K must be divisible by 128, got %lld", (long long)k);
+  DSV4_REQUIRE(shift_stride >= (k / 32 + 3) / 4, "b_shift2 stride mismatch (%lld < %lld)",
+               (long long)shift_stride, (long long)((k / 32 + 3) / 4));
+  return DSV4_OK;
+}
+
+int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_in,
+                    const uint8_t* b_mxfp4, const uint8_t* b_shift2, const float* cs,
+                    int64_t experts, int64_t n_rows, int64_t k, int64_t shift_stride, void* dst,
+                    int64_t ldo, int64_t tile_rows_y, int64_t inter,
+                    const int32_t* sorted_ids, int64_t sorted_cap, const int32_t* expert_ids,
+                    int64_t expert_cap, const int32_t* ntpp, int64_t topk, int64_t block_m,
+                    int src_is_slot, int64_t num_valid, int has_clamp, float clamp_limit,
+                    void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(a_q && a_scale && b_mxfp4 && b_shift2 && cs && dst && sorted_ids && expert_ids &&
+                   ntpp,
+               "null pointer argument");
+  if (int r = check_weights(experts, n_rows, k, shift_stride)) return r;
+  DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
+  DSV4_REQUIRE(block_m == 16 || block_m == 32 || block_m == 64 || block_m == 128,
+               "block_m must be 16, 32, 64, or 128, got %lld", (long long)block_m);
+  DSV4_REQUIRE(num_valid >= 0, "num_valid_tokens must be non-negative");
+  if (src_is_slot)
+    DSV4_REQUIRE(m_in >= num_valid, "W2 input rows do not cover routed slots");
+  else
+    DSV4_REQUIRE(m_in * topk >= num_valid, "W13 input rows do not cover routed slots");
+  const int64_t max_m = align_capacity(num_valid, experts, block_m);
+  const int64_t grid_m = (max_m + block_m - 1) / block_m;
+  DSV4_REQUIRE(sorted_cap >= max_m,
+               "sorted_token_ids capacity is smaller than maximum aligned token count");
+  DSV4_REQUIRE(expert_cap >= grid_m, "expert_ids capacity is smaller than maximum M tile count");
+  if (num_valid == 0 || grid_m == 0) return DSV4_OK;
+  DSV4_REQUIRE(grid_m <= 0x7FFFFFFF, "too many M tiles");
+
+  TcGemmParams p{};
+  p.a = a_q;
+  p.a_scale = a_scale;
+  p.lda = k;
+  p.a_rows = m_in;
+  p.b_packed = b_mxfp4;
+  p.b_shift = b_shift2;
+  p.cs = cs;
+  p.ng8 = static_cast<int>(n_rows / 8);
+  p.b_expert_stride = (k / 32) * p.ng8 * 128;
+  p.s_expert_stride = shift_stride * p.ng8 * 8;
+  p.n = static_cast<int>(n_rows);
+  p.inter = static_cast<int>(inter);
+  p.k_stages = static_cast<int>(k / 128);
+  p.stages_per_split = p.k_stages;
+  p.moe = 1;
+  p.sorted_ids = sorted_ids;
+  p.expert_ids = expert_ids;
+  p.ntpp = ntpp;
+  p.block_m = static_cast<int>(block_m);
+  p.topk = static_cast<int>(topk);
+  p.num_valid = static_cast<int>(num_valid);
+  p.src_is_slot = src_is_slot;
+  p.out = reinterpret_cast<__nv_bfloat16*>(dst);
+  p.ldo = ldo;
+  p.has_clamp = has_clamp;
+  p.clamp_limit = clamp_limit;
+  dim3 grid(static_cast<unsigned>(grid_m), static_cast<unsigned>(tile_rows_y), 1);
+  if (epi == kEpiSwiglu) return launch_gemm<kEpiSwiglu>(static_cast<int>(block_m), grid, p, as_stream(stream));
+  return launch_gemm<kEpiBf16>(static_cast<int>(block_m), grid, p, as_stream(stream));
+}
+
+int dense_tile(int64_t m) {
+  if (m <= 16) return 16;
+  if (m <= 32) return 32;
+  if (m <= 64) return 64;
+  if (m <= 128) return 128;
+  return 256;
+}
+
+int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
+                 const uint8_t* b_mxfp4, const uint8_t* b_shift2, int64_t shift_stride,
+                 const float* cs, int64_t n, void* out, int32_t* out_i32, int64_t splits,
+                 int64_t ld, int64_t split_stride, int epi, void* stream) {
+  if (int r = check_weights(1, n, k, shift_stride)) return r;
+  TcGemmParams p{};
+  p.a = a_q;
+  p.a_scale = a_scale;
+  p.lda = k;
+  p.a_rows = m;
+  p.b_packed = b_mxfp4;
+  p.b_shift = b_shift2;
+  p.cs = cs;
+  p.ng8 = static_cast<int>(n / 8);
+  p.b_expert_stride = 0;
+  p.s_expert_stride = 0;
+  p.n = static_cast<int>(n);
+  p.k_stages = static_cast<int>(k / 128);
+  p.stages_per_split = static_cast<int>((p.k_stages + splits - 1) / splits);
+  p.moe = 0;
+  p.m = static_cast<int>(m);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.out_i32 = out_i32;
+  p.ldo = ld;
+  p.split_stride = split_stride;
+  const int tn = dense_tile(m);
+  const int64_t gz = (p.k_stages + p.stages_per_split - 1) / p.stages_per_split;
+  dim3 grid(static_cast<unsigned>((m + tn - 1) / tn), static_cast<unsigned>(n / 128),
+            static_cast<unsigned>(gz));
+  if (epi == kEpiI32) return launch_gemm<kEpiI32>(tn, grid, p, as_stream(stream));
+  return launch_gemm<kEpiBf16>(tn, grid, p, as_stream(stream));
+}
+
+}  // namespace
+}  // namespace dsv4
+
+using namespace dsv4;
+
+extern "C" {
+
+int dsv4_b200_abi_version(void) { return DSV4_B200_ABI_VERSION; }
+
+const char* dsv4_b200_last_error(void) { return g_last_error; }
+
+int dsv4_b200_init(int device) {
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (device != prev) {
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+  }
+  int r = ensure_init();
+  if (device != prev) cudaSetDevice(prev);
+  return r;
+}
+
+int dsv4_b200_get_device_status(int* status, int reset) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(status != nullptr, "status is null");
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_device_status, sizeof(int));
+  if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "read status: %s", cudaGetErrorString(e));
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "reset status: %s", cudaGetErrorString(e));
+  }
+  return DSV4_OK;
+}
+
+int dsv4_b200_quantize_per_token_int8(const void* a, int dtype, int64_t m, int64_t k, int64_t lda,
+                                      float clamp_abs, int8_t* a_q, float* a_scale,
+                                      void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0 && k >= 0 && lda >= k, "bad shape m=%lld k=%lld lda=%lld", (long long)m,
+               (long long)k, (long long)lda);
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(a && a_q && a_scale, "null pointer argument");
+  const dim3 grid(static_cast<unsigned>((m + 7) / 8));
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case DSV4_F32:
+      quant_rows_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(a), m, k, lda,
+                                                     clamp_abs, a_q, a_scale);
+      break;
+    case DSV4_F16:
+      quant_rows_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(a), m, k, lda,
+                                                      clamp_abs, a_q, a_scale);
+      break;
+    case DSV4_BF16:
+      quant_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale);
+      break;
+    default:
+      return fail(DSV4_ERR_INVALID_ARGUMENT, "a must be fp32, fp16, or bf16 (dtype %d)", dtype);
+  }
+  return check_launch("quant_rows_kernel");
+}
+
+int dsv4_b200_remap_mxfp4_weight_for_int8(const uint8_t* weight, const uint8_t* scale,
+                                          int64_t experts, int64_t n, int64_t k,
+                                          int headroom_bits, int round_half_even,
+                                          uint8_t* b_mxfp4, uint8_t* b_shift2,
+                                          float* channel_scale, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(headroom_bits >= 0 && headroom_bits <= 7, "invalid headroom_bits=%d",
+               headroom_bits);
+  DSV4_REQUIRE(experts >= 0 && n >= 0 && k >= 0 && k % 32 == 0,
+               "expected K divisible by 32, got %lld", (long long)k);
+  if (experts == 0 || n == 0 || k == 0) return DSV4_OK;
+  DSV4_REQUIRE(weight && scale && b_mxfp4 && b_shift2 && channel_scale, "null pointer argument");
+  const int kb = static_cast<int>(k / 32);
+  const int ss = (kb + 3) / 4;
+  const int ng8 = static_cast<int>((n + 7) / 8);
+  cudaStream_t st = as_stream(stream);
+  // pad rows of the last 8-row group must read as zero
+  if (n % 8 != 0) {
+    cudaError_t e = cudaMemsetAsync(b_shift2, 0, experts * ss * ng8 * 8, st);
+    if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "memset: %s", cudaGetErrorString(e));
+  }
+  const int64_t rows = experts * n;
+  repack_channel_shift_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(
+      scale, rows, static_cast<int>(n), kb, ss, ng8, headroom_bits, channel_scale, b_shift2);
+  if (int r = check_launch("repack_channel_shift_kernel")) return r;
+  const int64_t words = experts * kb * ng8 * 32;
+  repack_codes_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, st>>>(
+      weight, scale, channel_scale, words, static_cast<int>(n), kb, ng8, headroom_bits,
+      round_half_even, reinterpret_cast<uint32_t*>(b_mxfp4));
+  return check_launch("repack_codes_kernel");
+}
+
+int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int64_t num_experts,
+                                   int64_t block_size, int32_t* sorted_token_ids,
+                                   int64_t sorted_capacity, int32_t* expert_ids,
+                                   int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
+                                   int32_t* cumsum_buffer, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(num_experts >= 1 && num_experts <= kAlignMaxExperts,
+               "num_experts must be in [1, %d], got %lld", kAlignMaxExperts,
+               (long long)num_experts);
+  DSV4_REQUIRE(block_size >= 1 && block_size <= 1024, "bad block_size %lld",
+               (long long)block_size);
+  DSV4_REQUIRE(numel >= 0 && numel < (1ll << 30), "bad numel %lld", (long long)numel);
+  DSV4_REQUIRE(num_tokens_post_pad && (topk_ids || numel == 0) &&
+                   (sorted_token_ids || sorted_capacity == 0) &&
+                   (expert_ids || expert_ids_capacity == 0),
+               "null pointer argument");
+  const int64_t need = align_capacity(numel, num_experts, block_size);
+  DSV4_REQUIRE(sorted_capacity >= need, "sorted_token_ids capacity %lld < %lld",
+               (long long)sorted_capacity, (long long)need);
+  DSV4_REQUIRE(expert_ids_capacity * block_size >= need, "expert_ids capacity too small");
+  const int smem = align_smem_bytes(static_cast<int>(num_experts));
+  moe_align_kernel<<<1, kAlignThreads, smem, as_stream(stream)>>>(
+      topk_ids, static_cast<int>(numel), static_cast<int>(num_experts),
+      static_cast<int>(block_size), sorted_token_ids, static_cast<int>(sorted_capacity),
+      expert_ids, static_cast<int>(expert_ids_capacity), num_tokens_post_pad, cumsum_buffer);
+  return check_launch("moe_align_kernel");
+}
+
+int dsv4_b200_mxfp4_int8_moe_gemm(const int8_t* a_q, const float* a_scale, int64_t m_in,
+                                  const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                  const float* b_channel_scale, int64_t num_experts, int64_t n,
+                                  int64_t k, int64_t shift_stride, void* dst,
+                                  const int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                  const int32_t* expert_ids, int64_t expert_ids_capacity,
+                                  const int32_t* num_tokens_post_padded, int64_t topk,
+                                  int64_t block_m, int source_rows_are_slots,
+                                  int64_t num_valid_tokens, void* stream) {
+  return moe_gemm_common(kEpiBf16, a_q, a_scale, m_in, b_mxfp4, b_shift2, b_channel_scale,
+                         num_experts, n, k, shift_stride, dst, n, n / 128, 0, sorted_token_ids,
+                         sorted_capacity, expert_ids, expert_ids_capacity, num_tokens_post_padded,
+                         topk, block_m, source_rows_are_slots ? 1 : 0, num_valid_tokens, 0, 0.f,
+                         stream);
+}
+
+int dsv4_b200_mxfp4_int8_moe_gemm_swiglu(
+    const int8_t* a_q, const float* a_scale, int64_t m_in, const uint8_t* b_mxfp4,
+    const uint8_t* b_shift2, const float* b_channel_scale, int64_t num_experts,
+    int64_t intermediate, int64_t k, int64_t shift_stride, void* out,
+    const int32_t* sorted_token_ids, int64_t sorted_capacity, const int32_t* expert_ids,
+    int64_t expert_ids_capacity, const int32_t* num_tokens_post_padded, int64_t topk,
+    int64_t block_m, int64_t num_valid_tokens, int has_clamp, float clamp_limit, void* stream) {
+  DSV4_REQUIRE(intermediate > 0 && intermediate % 64 == 0,
+               "intermediate_size must be a positive multiple of 64, got %lld",
+               (long long)intermediate);
+  return moe_gemm_common(kEpiSwiglu, a_q, a_scale, m_in, b_mxfp4, b_shift2, b_channel_scale,
+                         num_experts, 2 * intermediate, k, shift_stride, out, intermediate,
+                         intermediate / 64, intermediate, sorted_token_ids, sorted_capacity,
+                         expert_ids, expert_ids_capacity, num_tokens_post_padded, topk, block_m,
+                         0, num_valid_tokens, has_clamp, clamp_limit, stream);
+}
+
+int dsv4_b200_mxfp4_int8_moe_reduce(const void* routed_out, const float* topk_weights,
+                                    void* out, int64_t m_out, int64_t n, int64_t topk,
+                                    int64_t num_valid_tokens, int apply_scaling,
+                                    float routed_scaling_factor, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(n > 0 && n % 8 == 0, "reduce requires N divisible by 8, got %lld", (long long)n);
+  DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
+  DSV4_REQUIRE(num_valid_tokens >= 0, "num_valid_tokens must be non-negative");
+  DSV4_REQUIRE(m_out * topk >= num_valid_tokens, "out rows do not cover routed slots");
+  if (m_out == 0) return DSV4_OK;
+  DSV4_REQUIRE(routed_out && topk_weights && out, "null pointer argument");
+  const int64_t threads = m_out * (n / 8);
+  moe_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(routed_out), topk_weights,
+      static_cast<__nv_bfloat16*>(out), static_cast<int>(m_out), static_cast<int>(n),
+      static_cast<int>(topk), static_cast<int>(num_valid_tokens), routed_scaling_factor,
+      apply_scaling ? 1 : 0);
+  return check_launch("moe_reduce_kernel");
+}
+
+int dsv4_b200_mxfp4_int8_dense_gemm(const int8_t* a_q, const float* a_scale, int64_t m,
+                                    int64_t k, const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                    int64_t shift_stride, const float* b_channel_scale, int64_t n,
+                                    void* out, int32_t* partial, int64_t partial_splits,
+                                    int64_t partial_ld, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0, "bad m");
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(a_q && a_scale && b_mxfp4 && b_shift2 && b_channel_scale && out,
+               "null pointer argument");
+  DSV4_REQUIRE(m <= 0x7FFFFFFF, "m too large");
+  const int64_t k_stages = k / 128;
+  int64_t splits = 1;
+  if (partial != nullptr && m <= 128 && partial_splits >= 2 && k_stages >= 2) {
+    DSV4_REQUIRE(partial_ld >= n, "partial leading dimension %lld < N %lld",
+                 (long long)partial_ld, (long long)n);
+    const int64_t tiles = ((m + dense_tile(m) - 1) / dense_tile(m)) * (n / 128);
+    splits = sm_count() / (tiles > 0 ? tiles : 1);
+    if (splits < 2) splits = 2;
+    if (splits > partial_splits) splits = partial_splits;
+    if (splits > k_stages) splits = k_stages;
+    const int64_t sps = (k_stages + splits - 1) / splits;
+    splits = (k_stages + sps - 1) / sps;
+  }
+  if (splits > 1) {
+    const int64_t split_stride = m * partial_ld;
+    if (int r = dense_common(a_q, a_scale, m, k, b_mxfp4, b_shift2, shift_stride, b_channel_scale,
+                             n, nullptr, partial, splits, partial_ld, split_stride, kEpiI32,
+                             stream))
+      return r;
+    const int64_t total = m * n;
+    splitk_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0,
+                           as_stream(stream)>>>(partial, static_cast<int>(splits), split_stride,
+                                                partial_ld, a_scale, b_channel_scale,
+                                                static_cast<__nv_bfloat16*>(out),
+                                                static_cast<int>(m), static_cast<int>(n));
+    return check_launch("splitk_reduce_kernel");
+  }
+  return dense_common(a_q, a_scale, m, k, b_mxfp4, b_shift2, shift_stride, b_channel_scale, n,
+                      out, nullptr, 1, n, 0, kEpiBf16, stream);
+}
+
+int dsv4_b200_mxfp4_int8_dense_gemm_i32(const int8_t* a_q, int64_t m, int64_t k,
+                                        const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                        int64_t shift_stride, int64_t n, int32_t* acc,
+                                        void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0, "bad m");
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(a_q && b_mxfp4 && b_shift2 && acc, "null pointer argument");
+  return dense_common(a_q, nullptr, m, k, b_mxfp4, b_shift2, shift_stride, nullptr, n, nullptr,
+                      acc, 1, n, 0, kEpiI32, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,338 @@
+// Memory-bound kernels of the MoE path: per-token INT8 quantisation, expert
+// align (histogram / padded prefix sum / stable permutation), the load-time
+// MXFP4 -> INT8-decodable repack, the top-k combine and the dense split-K
+// reduce.
+#pragma once
+
+#include "common.cuh"
+
+namespace dsv4 {
+
+// ---------------------------------------------------------------------------
+// a1. per-token INT8 quantisation (reference PYMOE:53-126).
+// One warp per row.  scale = max|x| / 127 (IEEE division; 0 -> 1.0),
+// q = clamp(rne(x / scale), -127, 127).
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+__device__ __forceinline__ float clampf_abs(float x, float c) {
+  return c > 0.f ? fminf(fmaxf(x, -c), c) : x;
+}
+
+__device__ __forceinline__ int8_t quant1(float x, float s) {
+  int q = __float2int_rn(__fdiv_rn(x, s));
+  q = max(-127, min(127, q));
+  return static_cast<int8_t>(q);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ a, int64_t m,
+                                                         int64_t k, int64_t lda, float clamp_abs,
+                                                         int8_t* __restrict__ q,
+                                                         float* __restrict__ scale) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= m) return;
+  const T* x = a + row * lda;
+  int8_t* qr = q + row * k;
+  const bool vec = (sizeof(T) == 2) && (k % 8 == 0) && (lda % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(a) & 15) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
+  float amax = 0.f;
+  if (vec) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (int64_t i = lane; i < k / 8; i += 32) {
+      uint4 u = __ldg(xv + i);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(clampf_abs(to_f32<T>(e[j]), clamp_abs)));
+    }
+  } else {
+    for (int64_t i = lane; i < k; i += 32) amax = fmaxf(amax, fabsf(clampf_abs(to_f32<T>(x[i]), clamp_abs)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  float s = __fdiv_rn(amax, 127.0f);
+  if (s == 0.0f) s = 1.0f;
+  if (vec) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (int64_t i = lane; i < k / 8; i += 32) {
+      uint4 u = __ldg(xv + i);
+      const T* e = reinterpret_cast<const T*>(&u);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo |= (static_cast<uint32_t>(static_cast<uint8_t>(quant1(clampf_abs(to_f32<T>(e[j]), clamp_abs), s)))) << (8 * j);
+        hi |= (static_cast<uint32_t>(static_cast<uint8_t>(quant1(clampf_abs(to_f32<T>(e[j + 4]), clamp_abs), s)))) << (8 * j);
+      }
+      reinterpret_cast<uint2*>(qr)[i] = make_uint2(lo, hi);
+    }
+  } else {
+    for (int64_t i = lane; i < k; i += 32) qr[i] = quant1(clampf_abs(to_f32<T>(x[i]), clamp_abs), s);
+  }
+  if (lane == 0) scale[row] = s;
+}
+
+// ---------------------------------------------------------------------------
+// a5. expert align (reference call site PYMOE:842-869, library
+// sgl_kernel.moe_align_block_size).  One CTA of 1024 threads:
+//   1. each warp owns a contiguous segment of the flattened ids and counts
+//      its experts (shared atomics; counts are order-free),
+//   2. per expert: exclusive prefix over warps (stable placement bases),
+//   3. block-padded exclusive prefix over experts,
+//   4. each warp walks its segment in id order, 32 at a time; __match_any
+//      groups equal experts, the rank among lower lanes gives the position.
+// Result: inside an expert segment slot ids increase (stable order); padding
+// value is numel; ids outside [0, E) are dropped; expert_ids of blocks past
+// the padded total are -1.
+// ---------------------------------------------------------------------------
+constexpr int kAlignThreads = 1024;
+
+__global__ void __launch_bounds__(kAlignThreads, 1)
+moe_align_kernel(const int32_t* __restrict__ ids, int numel, int num_experts, int block_m,
+                 int32_t* __restrict__ sorted_ids, int sorted_cap, int32_t* __restrict__ expert_ids,
+                 int expert_cap, int32_t* __restrict__ ntpp, int32_t* __restrict__ cumsum_out) {
+  extern __shared__ int sm_align[];
+  const int E = num_experts;
+  int* wc = sm_align;             // [32][E] per-warp counts, then placement cursors
+  int* base = wc + 32 * E;        // [E + 1] padded exclusive prefix
+  int* wsum = base + E + 1;       // [32] scan scratch
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int seg = (numel + 31) / 32;
+  const int s_begin = min(numel, warp * seg);
+  const int s_end = min(numel, s_begin + seg);
+
+  for (int i = tid; i < 32 * E; i += kAlignThreads) wc[i] = 0;
+  __syncthreads();
+  for (int i = s_begin + lane; i < s_end; i += 32) {
+    const int e = __ldg(ids + i);
+    if (e >= 0 && e < E) atomicAdd(&wc[warp * E + e], 1);
+  }
+  __syncthreads();
+  // per-expert prefix over warps; expert total into base[e]
+  for (int e = tid; e < E; e += kAlignThreads) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wc[w * E + e];
+      wc[w * E + e] = run;
+      run += c;
+    }
+    base[e] = run;
+  }
+  __syncthreads();
+  // block-padded exclusive scan over experts (E <= 1024 -> one per thread)
+  {
+    const int cnt = tid < E ? base[tid] : 0;
+    const int padded = (cnt + block_m - 1) / block_m * block_m;
+    int v = padded;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) wsum[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int w = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      wsum[lane] = w;
+    }
+    __syncthreads();
+    const int incl = v + (warp > 0 ? wsum[warp - 1] : 0);
+    __syncthreads();
+    if (tid < E) base[tid] = incl - padded;
+    if (tid == E - 1) base[E] = incl;
+    if (E == 0 && tid == 0) base[0] = 0;
+  }
+  __syncthreads();
+  const int total = base[E];
+  for (int i = tid; i < sorted_cap; i += kAlignThreads) sorted_ids[i] = numel;
+  for (int b = tid; b < expert_cap; b += kAlignThreads) {
+    int e = -1;
+    const int pos = b * block_m;
+    if (pos < total) {
+      int lo = 0, hi = E - 1;  // last e with base[e] <= pos
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (base[mid] <= pos) lo = mid; else hi = mid - 1;
+      }
+      e = lo;
+    }
+    expert_ids[b] = e;
+  }
+  if (tid == 0) ntpp[0] = total;
+  if (cumsum_out != nullptr)
+    for (int e = tid; e <= E; e += kAlignThreads) cumsum_out[e] = base[e];
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int c = s_begin; c < s_end; c += 32) {
+    const int i = c + lane;
+    int e = i < s_end ? __ldg(ids + i) : -1;
+    const bool valid = e >= 0 && e < E;
+    const int key = valid ? e : (E + lane);  // unique key for invalid lanes
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int rank = __popc(peers & lt_mask);
+    if (valid) {
+      const int pos = base[e] + wc[warp * E + e] + rank;
+      if (pos < sorted_cap) sorted_ids[pos] = i;
+    }
+    __syncwarp();
+    if (valid && rank == 0) wc[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// a3. MXFP4 -> INT8-decodable repack (reference PYMOE:378-572 Triton kernels,
+// PYMOE:642-666 torch variant).  Load time only.
+// ---------------------------------------------------------------------------
+__global__ void repack_channel_shift_kernel(const uint8_t* __restrict__ scale, int64_t rows,
+                                            int n, int kb_count, int ss, int ng8, int headroom,
+                                            float* __restrict__ cs, uint8_t* __restrict__ shift2) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const uint8_t* sr = scale + row * kb_count;
+  int mx = -32768;
+  for (int kb = 0; kb < kb_count; ++kb) mx = max(mx, static_cast<int>(sr[kb]) - 127);
+  cs[row] = ldexpf(0.5f, mx - headroom);
+  const int64_t e = row / n;
+  const int nn = static_cast<int>(row - e * n);
+  const int g = nn >> 3, r = nn & 7;
+  for (int sb = 0; sb < ss; ++sb) {
+    uint32_t packed = 0;
+    for (int i = 0; i < 4; ++i) {
+      const int kb = sb * 4 + i;
+      if (kb < kb_count) {
+        const int delta = mx - (static_cast<int>(sr[kb]) - 127);
+        const int sh = min(3, max(0, headroom - delta));
+        packed |= static_cast<uint32_t>(sh) << (2 * i);
+      }
+    }
+    shift2[((e * ss + sb) * ng8 + g) * 8 + r] = static_cast<uint8_t>(packed);
+  }
+}
+
+__device__ __forceinline__ uint32_t remap_nibble(uint32_t nib, int exp, int max_exp, int headroom,
+                                                 int half_even) {
+  const uint32_t mag = nib & 7u;
+  const uint32_t sign = nib & 8u;
+  if (mag == 0) return 0u;
+  const float q_abs = static_cast<float>((0x0C08060403020100ull >> (8 * mag)) & 0xFF);
+  const int delta = max(max_exp - exp, 0);
+  const int shift = min(3, max(0, headroom - delta));
+  const float target = ldexpf(q_abs, headroom - delta);
+  float ti = half_even ? fminf(rintf(target), 128.0f) : floorf(target + 0.5f);
+  const float v = ldexpf(ti, -shift);
+  uint32_t m = 7;
+  if (v <= 10.0f) m = 6;
+  if (v <= 7.0f) m = 5;
+  if (v <= 5.0f) m = 4;
+  if (v <= 3.5f) m = 3;
+  if (v <= 2.5f) m = 2;
+  if (v <= 1.5f) m = 1;
+  if (v <= 0.5f) m = 0;
+  return m | sign;
+}
+
+// One thread per 32-bit word of the packed layout: (e, kb, g, lane).
+__global__ void repack_codes_kernel(const uint8_t* __restrict__ weight,
+                                    const uint8_t* __restrict__ scale,
+                                    const float* __restrict__ cs, int64_t total_words, int n,
+                                    int kb_count, int ng8, int headroom, int half_even,
+                                    uint32_t* __restrict__ out) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= total_words) return;
+  const int lane = static_cast<int>(w & 31);
+  const int64_t t1 = w >> 5;
+  const int g = static_cast<int>(t1 % ng8);
+  const int64_t t2 = t1 / ng8;
+  const int kb = static_cast<int>(t2 % kb_count);
+  const int64_t e = t2 / kb_count;
+  const int nn = g * 8 + (lane >> 2);
+  const int t = lane & 3;
+  uint32_t word = 0;
+  if (nn < n) {
+    const int64_t row = e * n + nn;
+    const int max_exp = ilogbf(cs[row]) + headroom + 1;
+    const int exp = static_cast<int>(scale[row * kb_count + kb]) - 127;
+    const uint8_t* src = weight + row * (kb_count * 16) + kb * 16;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int kk = (j < 2 ? 4 * t : 16 + 4 * t) + 2 * (j & 1);
+      const uint32_t byte = src[kk >> 1];
+      const uint32_t lo = remap_nibble(byte & 15u, exp, max_exp, headroom, half_even);
+      const uint32_t hi = remap_nibble(byte >> 4, exp, max_exp, headroom, half_even);
+      word |= (lo | (hi << 4)) << (8 * j);
+    }
+  }
+  out[w] = word;
+}
+
+// ---------------------------------------------------------------------------
+// a9. top-k combine (reference MOE_ENTRY:71-126) with the optional routed
+// scaling of PYMOE:957-958 fused: out = bf16(bf16(sum_k fma) * rsf).
+// One thread per (token, 8 columns).
+// ---------------------------------------------------------------------------
+__global__ void moe_reduce_kernel(const __nv_bfloat16* __restrict__ routed,
+                                  const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                  int m_out, int n, int topk, int num_valid, float rsf,
+                                  int apply_rsf) {
+  const int chunks = n / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(m_out) * chunks) return;
+  const int t = static_cast<int>(idx / chunks);
+  const int c = static_cast<int>(idx - static_cast<int64_t>(t) * chunks);
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    const int slot = t * topk + k;
+    if (slot >= num_valid) continue;
+    const float wt = __ldg(w + slot);
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(routed + static_cast<int64_t>(slot) * n) + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(__bfloat162float(e[i]), wt, acc[i]);
+  }
+  __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    __nv_bfloat16 b = __float2bfloat16_rn(acc[i]);
+    if (apply_rsf) b = __float2bfloat16_rn(__fmul_rn(__bfloat162float(b), rsf));
+    o[i] = b;
+  }
+  reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * n)[c] = *reinterpret_cast<uint4*>(o);
+}
+
+// Dense split-K reduce: out = bf16((f32(sum_s partial) * a[m]) * cs[n])
+// (reference DENSE_ENTRY:56-112).
+__global__ void splitk_reduce_kernel(const int32_t* __restrict__ partial, int splits,
+                                     int64_t split_stride, int64_t ld,
+                                     const float* __restrict__ a_scale,
+                                     const float* __restrict__ cs, __nv_bfloat16* __restrict__ out,
+                                     int m, int n) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(m) * n) return;
+  const int row = static_cast<int>(idx / n);
+  const int col = static_cast<int>(idx - static_cast<int64_t>(row) * n);
+  int32_t acc = 0;
+  for (int s = 0; s < splits; ++s) acc += __ldg(partial + s * split_stride + row * ld + col);
+  const float v = __fmul_rn(__fmul_rn(__int2float_rn(acc), __ldg(a_scale + row)), __ldg(cs + col));
+  out[idx] = __float2bfloat16_rn(v);
+}
+
+}  // namespace dsv4

@@ -1,0 +1,305 @@
+"""MXFP4-weight / INT8-activation MoE and dense ops for B200 (sm_100a).
+
+Drop-in mirror of the reference's op layer
+``dsv4_a100_patch/triton_kernels/mxfp4_int8_moe.py`` (PYMOE): the same public
+names, arguments, returned layouts and error types, backed by the C ABI of
+``libdsv4_b200.so`` (hand-written sm_100a kernels).  There is no CPU path: a
+CPU tensor or a missing library raises.
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+
+import torch
+from torch.nn import Parameter
+
+from . import _native as N
+from .jit_ops import (
+    mxfp4_int8_moe_gemm_swiglu,
+    mxfp4_int8_moe_gemm,
+    mxfp4_int8_moe_reduce,
+    mxfp4_int8_dense_gemm,
+    prewarm_mxfp4_int8_moe_jit_modules,
+)
+
+_VALID_BLOCK_M = {16, 32, 64, 128}
+_VALID_BLOCK_N = {32, 64, 128}
+_MAX_BLOCK_M = 128
+# The B200 kernel computes 128 output channels per CTA; block_n is kept in the
+# API for compatibility and does not change the tile.
+_B200_BLOCK_N = 128
+
+
+@dataclass
+class Mxfp4Int8MoeWeights:
+    """PYMOE:34-43."""
+    w13_mxfp4: torch.Tensor
+    w13_shift2: torch.Tensor
+    w13_channel_scale: torch.Tensor
+    w2_mxfp4: torch.Tensor
+    w2_shift2: torch.Tensor
+    w2_channel_scale: torch.Tensor
+    headroom_bits: int
+
+
+@dataclass
+class Mxfp4Int8DenseWeight:
+    """PYMOE:46-50."""
+    weight_mxfp4: torch.Tensor
+    weight_shift2: torch.Tensor
+    weight_channel_scale: torch.Tensor
+    headroom_bits: int
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor on an sm_100a device (no CPU path)")
+
+
+_DTYPES = {torch.float32: N.DTYPE_F32, torch.float16: N.DTYPE_F16, torch.bfloat16: N.DTYPE_BF16}
+
+
+def quantize_per_token_int8(a: torch.Tensor, clamp_abs: float = 0.0):
+    """PYMOE:95-126: ``(q int8 [M,K], scale fp32 [M])``."""
+    if a.dim() != 2:
+        raise ValueError(f"a must have shape [M, K], got {tuple(a.shape)}")
+    if a.dtype not in _DTYPES:
+        raise TypeError(f"a must be fp32, fp16, or bf16, got {a.dtype}")
+    _require_cuda(a, "a")
+    a = a.contiguous()
+    m, k = a.shape
+    a_q = torch.empty((m, k), device=a.device, dtype=torch.int8)
+    a_scale = torch.empty((m,), device=a.device, dtype=torch.float32)
+    N.call("dsv4_b200_quantize_per_token_int8", a.data_ptr(), _DTYPES[a.dtype], m, k, k,
+           float(clamp_abs), a_q.data_ptr(), a_scale.data_ptr(), N.stream_of(a))
+    return a_q, a_scale
+
+
+def _as_uint8_storage(tensor: torch.Tensor) -> torch.Tensor:
+    """PYMOE:269-279."""
+    data = tensor.data if hasattr(tensor, "data") else tensor
+    if data.dtype == torch.uint8:
+        return data.contiguous()
+    if data.dtype == torch.int8:
+        return data.view(torch.uint8).contiguous()
+    if data.dtype == torch.float8_e8m0fnu:
+        return data.view(torch.uint8).contiguous()
+    if data.dtype in (torch.float16, torch.bfloat16, torch.float32):
+        return data.to(torch.float8_e8m0fnu).view(torch.uint8).contiguous()
+    raise TypeError(f"unsupported MXFP4 scale dtype: {data.dtype}")
+
+
+def remap_mxfp4_weight_for_int8(weight: torch.Tensor, scale: torch.Tensor, *, headroom_bits: int = 3,
+                                use_triton: bool = True):
+    """PYMOE:607-667.  ``use_triton=True`` selects the production rounding of
+    the reference's Triton repack (half-up), ``False`` its torch repack
+    (half-even); both run on the GPU here."""
+    if headroom_bits < 0 or headroom_bits > 7:
+        raise ValueError(f"invalid headroom_bits={headroom_bits}")
+    w_u8 = weight.data if hasattr(weight, "data") else weight
+    w_u8 = w_u8.view(torch.uint8).contiguous()
+    scale_u8 = _as_uint8_storage(scale)
+    if w_u8.dim() != 3 or scale_u8.dim() != 3:
+        raise ValueError(
+            f"expected expert weight/scale shapes [E, N, K/2] and [E, N, K/32], "
+            f"got {tuple(w_u8.shape)} and {tuple(scale_u8.shape)}")
+    if w_u8.shape[0] != scale_u8.shape[0] or w_u8.shape[1] != scale_u8.shape[1]:
+        raise ValueError(f"weight/scale shape mismatch: {tuple(w_u8.shape)} vs {tuple(scale_u8.shape)}")
+    if w_u8.shape[2] * 2 != scale_u8.shape[2] * 32:
+        raise ValueError(f"K mismatch: {tuple(w_u8.shape)} vs {tuple(scale_u8.shape)}")
+    _require_cuda(w_u8, "weight")
+    e, n, pk = w_u8.shape
+    k = pk * 2
+    kb = k // 32
+    ng8 = (n + 7) // 8
+    ss = (kb + 3) // 4
+    b_mxfp4 = torch.empty((e, kb, ng8, 128), device=w_u8.device, dtype=torch.uint8)
+    b_shift2 = torch.empty((e, ss, ng8, 8), device=w_u8.device, dtype=torch.uint8)
+    cs = torch.empty((e, n), device=w_u8.device, dtype=torch.float32)
+    N.call("dsv4_b200_remap_mxfp4_weight_for_int8", w_u8.data_ptr(), scale_u8.data_ptr(), e, n, k,
+           headroom_bits, 0 if use_triton else 1, b_mxfp4.data_ptr(), b_shift2.data_ptr(),
+           cs.data_ptr(), N.stream_of(w_u8))
+    return b_mxfp4, b_shift2, cs
+
+
+def prepare_mxfp4_int8_dense_weight(weight: torch.Tensor, scale: torch.Tensor, *,
+                                    headroom_bits: int = 3) -> Mxfp4Int8DenseWeight:
+    """PYMOE:670-686."""
+    b, sh, cs = remap_mxfp4_weight_for_int8(weight.unsqueeze(0), scale.unsqueeze(0),
+                                            headroom_bits=headroom_bits)
+    return Mxfp4Int8DenseWeight(b[0].contiguous(), sh[0].contiguous(), cs[0].contiguous(),
+                                headroom_bits)
+
+
+def mxfp4_int8_dense_forward(hidden_states: torch.Tensor, weight: Mxfp4Int8DenseWeight,
+                             bias: torch.Tensor | None = None) -> torch.Tensor:
+    """PYMOE:689-740 (bias unsupported, as in the reference)."""
+    if bias is not None:
+        raise NotImplementedError("MXFP4-int8 dense JIT path does not support bias")
+    hidden_states = hidden_states.contiguous()
+    a_q, a_scale = quantize_per_token_int8(hidden_states, 0.0)
+    n = weight.weight_channel_scale.shape[0]
+    m = hidden_states.shape[0]
+    out = torch.empty((m, n), device=hidden_states.device, dtype=torch.bfloat16)
+    partial = (torch.empty((4, m, (n + 31) // 32 * 32), device=hidden_states.device, dtype=torch.int32)
+               if m <= 128 else torch.empty((0,), device=hidden_states.device, dtype=torch.int32))
+    mxfp4_int8_dense_gemm(a_q, a_scale, weight.weight_mxfp4, weight.weight_shift2,
+                          weight.weight_channel_scale, out, partial)
+    return out
+
+
+def prepare_mxfp4_int8_moe(layer: torch.nn.Module, *, headroom_bits: int = 3,
+                           topk: int | None = None) -> None:
+    """PYMOE:743-788: repack W13/W2, prewarm, free the original Parameters."""
+    backend = os.environ.get("SGLANG_DSV4_MXFP4_INT8_REPACK_BACKEND", "triton").strip().lower()
+    if backend not in {"triton", "torch"}:
+        raise ValueError("SGLANG_DSV4_MXFP4_INT8_REPACK_BACKEND must be 'triton' or 'torch'")
+    use_triton = backend == "triton"
+    w13 = remap_mxfp4_weight_for_int8(layer.w13_weight.data, layer.w13_weight_scale_inv.data,
+                                      headroom_bits=headroom_bits, use_triton=use_triton)
+    w2 = remap_mxfp4_weight_for_int8(layer.w2_weight.data, layer.w2_weight_scale_inv.data,
+                                     headroom_bits=headroom_bits, use_triton=use_triton)
+    layer._dsv4_mxfp4_int8_weights = Mxfp4Int8MoeWeights(*w13, *w2, headroom_bits)
+    if topk is None:
+        topk = int(getattr(layer, "top_k", 0) or getattr(layer, "topk", 0) or 8)
+    hidden_size = int(w2[2].shape[1])
+    intermediate_size = int(w2[0].shape[1] * 32)
+    prewarm_mxfp4_int8_moe_jit_modules(hidden_size=hidden_size,
+                                       intermediate_size=intermediate_size, topk=topk)
+    empty_u8 = torch.empty(0, device=w13[0].device, dtype=torch.uint8)
+    empty_i8 = empty_u8.view(torch.int8)
+    layer.w13_weight = Parameter(empty_i8, requires_grad=False)
+    layer.w2_weight = Parameter(empty_i8, requires_grad=False)
+    layer.w13_weight_scale_inv = Parameter(empty_u8, requires_grad=False)
+    layer.w2_weight_scale_inv = Parameter(empty_u8, requires_grad=False)
+
+
+def max_mxfp4_int8_moe_block_m(m: int, topk: int, experts: int) -> int:
+    """PYMOE:799-801."""
+    avg = max(1, (m * topk + max(experts, 1) - 1) // max(experts, 1))
+    return min(_MAX_BLOCK_M, max(16, 1 << (avg - 1).bit_length()))
+
+
+def _parse_tile_shape(text: str) -> tuple[int, int]:
+    parts = text.strip().lower().replace("x", ",").split(",")
+    if len(parts) != 2:
+        raise ValueError(f"invalid tile shape {text!r}, expected MxN")
+    block_m, block_n = int(parts[0]), int(parts[1])
+    if block_m not in _VALID_BLOCK_M:
+        raise ValueError("block_m must be 16, 32, 64, or 128")
+    if block_n not in _VALID_BLOCK_N:
+        raise ValueError("block_n must be 32, 64, or 128")
+    return block_m, block_n
+
+
+def _select_moe_tile_shape(m: int, topk: int, experts: int) -> tuple[int, int]:
+    """B200 tile policy with the reference's env overrides and cap
+    (PYMOE:816-839).  The token tile equals block_m and one decoded weight
+    tile serves all of its tokens, so the largest block_m under the cap
+    (the average routed tokens per expert, rounded up to a power of two)
+    is chosen."""
+    max_block_m = max_mxfp4_int8_moe_block_m(m, topk, experts)
+    bm_env = os.environ.get("SGLANG_DSV4_MXFP4_INT8_BLOCK_M", "").strip()
+    bn_env = os.environ.get("SGLANG_DSV4_MXFP4_INT8_BLOCK_N", "").strip()
+    if bm_env or bn_env:
+        block_m = int(bm_env) if bm_env else 16
+        block_n = int(bn_env) if bn_env else 128
+        if block_m not in _VALID_BLOCK_M:
+            raise ValueError("SGLANG_DSV4_MXFP4_INT8_BLOCK_M must be 16, 32, 64, or 128")
+        if block_n not in _VALID_BLOCK_N:
+            raise ValueError("SGLANG_DSV4_MXFP4_INT8_BLOCK_N must be 32, 64, or 128")
+        if block_m > max_block_m:
+            raise ValueError(f"SGLANG_DSV4_MXFP4_INT8_BLOCK_M={block_m} exceeds cap "
+                             f"{max_block_m} for m={m}, topk={topk}, experts={experts}")
+        return block_m, block_n
+    return max_block_m, _B200_BLOCK_N
+
+
+def select_mxfp4_int8_moe_tile_shape(m: int, topk: int, experts: int) -> tuple[int, int]:
+    """PYMOE:795-796."""
+    return _select_moe_tile_shape(m, topk, experts)
+
+
+def align_capacity(numel: int, num_experts: int, block_size: int) -> int:
+    """PYMOE:848-851."""
+    if numel < num_experts + 1:
+        return numel * block_size
+    return numel + (num_experts + 1) * (block_size - 1)
+
+
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int):
+    """Native replacement of ``_moe_align_block_size`` (PYMOE:842-869):
+    ``(sorted_token_ids, expert_ids, num_tokens_post_pad)``.  Stable order
+    inside each expert; padding value ``numel``; ids outside [0, E) dropped."""
+    _require_cuda(topk_ids, "topk_ids")
+    ids = topk_ids.to(torch.int32).contiguous()
+    numel = ids.numel()
+    cap = align_capacity(numel, num_experts, block_size)
+    dev = ids.device
+    sorted_ids = torch.empty((cap,), dtype=torch.int32, device=dev)
+    n_blocks = (cap + block_size - 1) // block_size
+    expert_ids = torch.empty((n_blocks,), dtype=torch.int32, device=dev)
+    ntpp = torch.empty((1,), dtype=torch.int32, device=dev)
+    N.call("dsv4_b200_moe_align_block_size", ids.data_ptr() if numel else None, numel, num_experts,
+           block_size, sorted_ids.data_ptr(), cap, expert_ids.data_ptr(), n_blocks,
+           ntpp.data_ptr(), None, N.stream_of(ids))
+    return sorted_ids, expert_ids, ntpp
+
+
+_moe_align_block_size = moe_align_block_size
+
+
+def _apply_swiglu(x: torch.Tensor, clamp_limit: float | None) -> torch.Tensor:
+    """PYMOE:872-877 (kept for callers of the unfused path)."""
+    gate, up = x.chunk(2, dim=-1)
+    if clamp_limit is not None:
+        gate = gate.clamp(max=clamp_limit)
+        up = up.clamp(min=-clamp_limit, max=clamp_limit)
+    return torch.nn.functional.silu(gate) * up
+
+
+def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWeights,
+                           topk_ids: torch.Tensor, topk_weights: torch.Tensor, *, hidden_size: int,
+                           intermediate_size: int, routed_scaling_factor: float | None = None,
+                           clamp_limit: float | None = None,
+                           apply_router_weight_on_input: bool = False) -> torch.Tensor:
+    """PYMOE:880-959.  Launches: align, quant, W13 GEMM with fused SwiGLU,
+    quant, W2 GEMM, top-k combine with the routed scaling fused."""
+    if apply_router_weight_on_input:
+        raise NotImplementedError(
+            "mxfp4_int8 MoE only supports router weights in the W2 reduce path")
+    if hidden_states.dtype != torch.bfloat16:
+        hidden_states = hidden_states.to(torch.bfloat16)
+    hidden_states = hidden_states.contiguous()
+    _require_cuda(hidden_states, "hidden_states")
+    topk_ids_i32 = topk_ids.to(torch.int32).contiguous()
+    topk_weights_f32 = topk_weights.to(torch.float32).contiguous()
+    m = hidden_states.shape[0]
+    topk = topk_ids_i32.shape[1]
+    experts = weights.w13_mxfp4.shape[0]
+    block_m, block_n = _select_moe_tile_shape(m, topk, experts)
+    sorted_ids, expert_ids, ntpp = moe_align_block_size(topk_ids_i32, block_m, experts)
+    a13_q, a13_scale = quantize_per_token_int8(hidden_states, 0.0)
+    inter = torch.empty((m * topk, intermediate_size), device=hidden_states.device,
+                        dtype=torch.bfloat16)
+    mxfp4_int8_moe_gemm_swiglu(
+        a13_q, a13_scale, weights.w13_mxfp4, weights.w13_shift2, weights.w13_channel_scale,
+        inter, sorted_ids, expert_ids, ntpp, hidden_size=hidden_size,
+        intermediate_size=intermediate_size, topk=topk, block_m=block_m,
+        num_valid_tokens=m * topk, clamp_limit=clamp_limit)
+    a2_q, a2_scale = quantize_per_token_int8(inter, 0.0)
+    out = torch.empty((m, hidden_size), device=hidden_states.device, dtype=torch.bfloat16)
+    routed_out = torch.empty((m * topk, hidden_size), device=hidden_states.device,
+                             dtype=torch.bfloat16)
+    mxfp4_int8_moe_gemm(
+        a2_q, a2_scale, weights.w2_mxfp4, weights.w2_shift2, weights.w2_channel_scale, out,
+        topk_weights_f32, sorted_ids, expert_ids, ntpp, hidden_size=hidden_size,
+        intermediate_size=intermediate_size, topk=topk, block_m=block_m, block_n=block_n,
+        source_rows_are_slots=True, num_valid_tokens=m * topk, routed_out=routed_out)
+    mxfp4_int8_moe_reduce(routed_out, topk_weights_f32, out, hidden_size=hidden_size,
+                          intermediate_size=intermediate_size, topk=topk, block_m=block_m,
+                          block_n=block_n, num_valid_tokens=m * topk,
+                          routed_scaling_factor=routed_scaling_factor)
+    return out

@@ -1,0 +1,162 @@
+/*
+ * dsv4_b200.h -- C ABI of the B200 (sm_100a) MXFP4-weight / INT8-activation
+ * MoE hot path.
+ *
+ * Plain pointers and sizes only.  Every buffer is caller-allocated device
+ * memory (the library allocates nothing on the call path); every call is
+ * asynchronous on `stream` (a cudaStream_t passed as void*, NULL = legacy
+ * default stream) and returns a dsv4_status.  On failure
+ * dsv4_b200_last_error() returns a message for the calling thread.
+ *
+ * Each entry point names the interface of Qeeweew/deepseek-v4-a100-sglang it
+ * replaces (file:line, relative to that project's root).  Short names:
+ *   PYMOE       dsv4_a100_patch/triton_kernels/mxfp4_int8_moe.py
+ *   JITMOE      dsv4_a100_patch/sglang_jit_patches/mxfp4_int8_moe.py
+ *   JITDENSE    dsv4_a100_patch/sglang_jit_patches/mxfp4_int8_dense.py
+ *   MOE_ENTRY   dsv4_a100_patch/sglang_jit_patches/csrc/gemm/mxfp4_int8/mxfp4_int8_moe_entry.cuh
+ *   DENSE_ENTRY dsv4_a100_patch/sglang_jit_patches/csrc/gemm/mxfp4_int8/mxfp4_int8_dense_entry.cuh
+ *
+ * Weight layout (the reference's repacked format, PYMOE:290-333, 477-518):
+ *   b_mxfp4  u8  [E][K/32][ceil(N/8)][128]   remapped FP4 codes, lane order
+ *   b_shift2 u8  [E][shift_stride][ceil(N/8)][8], 2-bit shift per 32-K block
+ *   b_channel_scale f32 [E][N]
+ */
+#ifndef DSV4_B200_H
+#define DSV4_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSV4_API __attribute__((visibility("default")))
+#else
+#define DSV4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum dsv4_status {
+  DSV4_OK = 0,
+  DSV4_ERR_INVALID_ARGUMENT = 1, /* maps to RuntimeError (the reference RuntimeCheck) */
+  DSV4_ERR_UNSUPPORTED = 2,      /* maps to NotImplementedError */
+  DSV4_ERR_CUDA = 3,             /* maps to RuntimeError */
+  DSV4_ERR_DEVICE = 4            /* a kernel gave up a bounded wait */
+} dsv4_status;
+
+typedef enum dsv4_dtype { DSV4_F32 = 0, DSV4_F16 = 1, DSV4_BF16 = 2 } dsv4_dtype;
+
+#define DSV4_B200_ABI_VERSION 1
+
+DSV4_API int dsv4_b200_abi_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+DSV4_API const char* dsv4_b200_last_error(void);
+
+/* Kernel attributes (dynamic shared memory) for `device`; call once per
+ * device before CUDA-graph capture.  Replaces init_mxfp4_int8_moe_attrs and
+ * init_mxfp4_int8_dense_attrs (JITMOE:91-105 -> MOE_ENTRY:142-144;
+ * JITDENSE:47-56 -> DENSE_ENTRY:321-332). */
+DSV4_API int dsv4_b200_init(int device);
+
+/* Device status word written by kernels that abandoned a bounded wait
+ * (0 = none).  `reset` != 0 clears it.  Synchronous. */
+DSV4_API int dsv4_b200_get_device_status(int* status, int reset);
+
+/* a1. Per-token INT8 quantisation: scale = max|x|/127 (0 -> 1), q =
+ * clamp(rne(x/scale), +-127); optional |x| clamp first.  Replaces
+ * quantize_per_token_int8 / _quantize_per_token_kernel (PYMOE:53-126).
+ * a: [m][k] with row stride lda (elements), dtype dsv4_dtype; a_q: [m][k]. */
+DSV4_API int dsv4_b200_quantize_per_token_int8(const void* a, int dtype, int64_t m, int64_t k,
+                                      int64_t lda, float clamp_abs, int8_t* a_q,
+                                      float* a_scale, void* stream);
+
+/* a3. Repack packed MXFP4 [E][N][K/2] + UE8M0 scales [E][N][K/32] into the
+ * INT8-decodable format.  round_half_even = 0 follows the production Triton
+ * repack (PYMOE:378-572), 1 the torch repack (PYMOE:642-666).  Replaces
+ * remap_mxfp4_weight_for_int8 (PYMOE:607-667).  K % 32 == 0. */
+DSV4_API int dsv4_b200_remap_mxfp4_weight_for_int8(const uint8_t* weight, const uint8_t* scale,
+                                          int64_t experts, int64_t n, int64_t k,
+                                          int headroom_bits, int round_half_even,
+                                          uint8_t* b_mxfp4, uint8_t* b_shift2,
+                                          float* channel_scale, void* stream);
+
+/* a5. Expert histogram + block-padded prefix sum + stable permutation.
+ * Replaces the sgl_kernel.moe_align_block_size call of
+ * _moe_align_block_size (PYMOE:842-869).  topk_ids int32 [numel]; experts
+ * <= 1024; sorted_token_ids [sorted_capacity] (padding value numel);
+ * expert_ids [expert_ids_capacity] (-1 past the padded total);
+ * num_tokens_post_pad [1]; cumsum_buffer [num_experts + 1] or NULL. */
+DSV4_API int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int64_t num_experts,
+                                   int64_t block_size, int32_t* sorted_token_ids,
+                                   int64_t sorted_capacity, int32_t* expert_ids,
+                                   int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
+                                   int32_t* cumsum_buffer, void* stream);
+
+/* a6/a8. Grouped MXFP4 x INT8 GEMM over the aligned permutation:
+ *   dst[slot][n] = bf16((f32(sum_k a_q[src][k] * W[e][n][k]) * a_scale[src]) * cs[e][n])
+ * src = slot (source_rows_are_slots, W2) or slot / topk (W13).  dst has
+ * num_valid_tokens rows of n bf16 (W13: the gate_up output; W2: the
+ * routed_out workspace).  Replaces mxfp4_int8_moe_gemm (JITMOE:143-192 ->
+ * MOE_ENTRY:146-272).  block_m in {16,32,64,128}; n % 128 == 0;
+ * k % 128 == 0. */
+DSV4_API int dsv4_b200_mxfp4_int8_moe_gemm(const int8_t* a_q, const float* a_scale, int64_t m_in,
+                                  const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                  const float* b_channel_scale, int64_t num_experts, int64_t n,
+                                  int64_t k, int64_t shift_stride, void* dst,
+                                  const int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                  const int32_t* expert_ids, int64_t expert_ids_capacity,
+                                  const int32_t* num_tokens_post_padded, int64_t topk,
+                                  int64_t block_m, int source_rows_are_slots,
+                                  int64_t num_valid_tokens, void* stream);
+
+/* a6+a7. W13 grouped GEMM with the SwiGLU of _apply_swiglu (PYMOE:872-877)
+ * fused into the epilogue: gate_up is rounded to bf16 exactly as the
+ * reference's gate_up tensor, then silu(min(gate, L)) * clamp(up, -L, L) in
+ * bf16 arithmetic.  out: [num_valid_tokens][intermediate] bf16.  Replaces
+ * the W13 call + _apply_swiglu of mxfp4_int8_moe_forward (PYMOE:916-935).
+ * has_clamp = 0 disables the limit.  intermediate % 64 == 0. */
+DSV4_API int dsv4_b200_mxfp4_int8_moe_gemm_swiglu(
+    const int8_t* a_q, const float* a_scale, int64_t m_in, const uint8_t* b_mxfp4,
+    const uint8_t* b_shift2, const float* b_channel_scale, int64_t num_experts,
+    int64_t intermediate, int64_t k, int64_t shift_stride, void* out,
+    const int32_t* sorted_token_ids, int64_t sorted_capacity, const int32_t* expert_ids,
+    int64_t expert_ids_capacity, const int32_t* num_tokens_post_padded, int64_t topk,
+    int64_t block_m, int64_t num_valid_tokens, int has_clamp, float clamp_limit, void* stream);
+
+/* a9. Top-k combine: out[t][n] = bf16(sum_k f32(routed_out[t*topk+k][n]) *
+ * w[t][k]) over slots < num_valid_tokens, fma in k order; then, if
+ * apply_scaling, out = bf16(out * routed_scaling_factor).  Replaces
+ * mxfp4_int8_moe_reduce (JITMOE:196-225 -> MOE_ENTRY:274-321) and
+ * out.mul_(routed_scaling_factor) (PYMOE:957-958).  n % 8 == 0. */
+DSV4_API int dsv4_b200_mxfp4_int8_moe_reduce(const void* routed_out, const float* topk_weights,
+                                    void* out, int64_t m_out, int64_t n, int64_t topk,
+                                    int64_t num_valid_tokens, int apply_scaling,
+                                    float routed_scaling_factor, void* stream);
+
+/* a11. Dense MXFP4 x INT8 GEMM: out[m][n] = bf16((f32(acc) * a_scale[m]) *
+ * cs[n]).  `partial` (int32 [partial_splits][m][partial_ld]) is the
+ * caller-provided split-K workspace used when m <= 128 (NULL disables
+ * split-K).  Replaces mxfp4_int8_dense_gemm (JITDENSE:73-108 ->
+ * DENSE_ENTRY:334-433).  b_mxfp4 [K/32][ceil(N/8)][128], b_shift2
+ * [shift_stride][ceil(N/8)][8]; n % 128 == 0; k % 128 == 0. */
+DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm(const int8_t* a_q, const float* a_scale, int64_t m,
+                                    int64_t k, const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                    int64_t shift_stride, const float* b_channel_scale, int64_t n,
+                                    void* out, int32_t* partial, int64_t partial_splits,
+                                    int64_t partial_ld, void* stream);
+
+/* Dense GEMM that writes the raw int32 accumulators acc[m][n] (row stride
+ * n).  Verification hook for the int32 bit-exactness of the tensor-core
+ * path; it is the split-K partial kernel of mxfp4_int8_dense_gemm run with a
+ * single split (DENSE_ENTRY:374-407 writes the same quantity). */
+DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm_i32(const int8_t* a_q, int64_t m, int64_t k,
+                                        const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                        int64_t shift_stride, int64_t n, int32_t* acc,
+                                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV4_B200_H */
