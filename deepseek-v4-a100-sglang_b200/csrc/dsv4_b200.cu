@@ -237,6 +237,33 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   return launch_gemm<kEpiBf16>(tn, grid, p, as_stream(stream));
 }
 
+// Fixed split-K workspace of dsv4_b200_mxfp4_int8_dense_gemm_noalloc:
+// 4 splits x 128 rows x 4096 columns of int32 (8 MiB) per device that loads
+// the library, held until process exit.  In host code `g_noalloc_splitk` is
+// only a stand-in symbol; the kernels get the address from
+// cudaGetSymbolAddress (noalloc_scratch()).
+constexpr int64_t kNoAllocScratchWords = 4ll * 128 * 4096;
+static __device__ __align__(256) int32_t g_noalloc_splitk[kNoAllocScratchWords];
+int32_t* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(DSV4_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_splitk);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(DSV4_ERR_CUDA, "cudaGetSymbolAddress(split-K workspace): %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return DSV4_OK;
+}
+
 }  // namespace
 }  // namespace dsv4
 
@@ -468,6 +495,28 @@ int dsv4_b200_mxfp4_int8_dense_gemm_i32(const int8_t* a_q, int64_t m, int64_t k,
   DSV4_REQUIRE(a_q && b_mxfp4 && b_shift2 && acc, "null pointer argument");
   return dense_common(a_q, nullptr, m, k, b_mxfp4, b_shift2, shift_stride, nullptr, n, nullptr,
                       acc, 1, n, 0, kEpiI32, stream);
+}
+
+// Allocation-free variant of dsv4_b200_mxfp4_int8_dense_gemm: the split-K
+// workspace is the library's fixed device array (see the header for limits
+// and the sharing rule).  Runs the same kernels as the allocating entry.
+int dsv4_b200_mxfp4_int8_dense_gemm_noalloc(const int8_t* a_q, const float* a_scale, int64_t m,
+                                            int64_t k, const uint8_t* b_mxfp4,
+                                            const uint8_t* b_shift2, int64_t shift_stride,
+                                            const float* b_channel_scale, int64_t n, void* out,
+                                            void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0 && n > 0, "bad shape m=%lld n=%lld", (long long)m, (long long)n);
+  const int64_t ld = (n + 31) / 32 * 32;
+  const int64_t splits = 4;
+  DSV4_REQUIRE(m <= 128 && splits * m * ld <= kNoAllocScratchWords,
+               "dense_gemm_noalloc: m=%lld, n=%lld exceed the fixed split-K workspace "
+               "(m <= 128 and 4*m*ceil32(n) <= %lld int32 words)",
+               (long long)m, (long long)n, (long long)kNoAllocScratchWords);
+  int32_t* scratch = nullptr;
+  if (int r = noalloc_scratch(&scratch)) return r;
+  return dsv4_b200_mxfp4_int8_dense_gemm(a_q, a_scale, m, k, b_mxfp4, b_shift2, shift_stride,
+                                         b_channel_scale, n, out, scratch, splits, ld, stream);
 }
 
 }  // extern "C"

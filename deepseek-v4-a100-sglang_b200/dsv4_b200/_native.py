@@ -43,6 +43,8 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_mxfp4_int8_dense_gemm": [_P, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _P,
                                         _I64, _I64, _P],
     "dsv4_b200_mxfp4_int8_dense_gemm_i32": [_P, _I64, _I64, _P, _P, _I64, _I64, _P, _P],
+    "dsv4_b200_mxfp4_int8_dense_gemm_noalloc": [_P, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P,
+                                                _P],
 }
 _RESTYPES = {"dsv4_b200_last_error": ctypes.c_char_p}
 

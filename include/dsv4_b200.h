@@ -155,6 +155,28 @@ DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm_i32(const int8_t* a_q, int64_t m, i
                                         int64_t shift_stride, int64_t n, int32_t* acc,
                                         void* stream);
 
+/* Dense MXFP4 x INT8 GEMM for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Same math and arguments as
+ * mxfp4_int8_dense_gemm, but the split-K workspace that the small-M path
+ * needs comes from a fixed array inside this library instead of from the
+ * caller: code running where cudaMalloc is forbidden or unavailable (a
+ * custom allocator that owns all device memory, a plugin host that hands
+ * out only its own buffers, code between CUDA-graph-recorded steps that must
+ * not touch the allocator) can still call it.  The caller passes inputs and
+ * `out`.  Limits: m <= 128 and 4 * m * ceil32(n) <= 2,097,152 int32 words
+ * (8 MiB, e.g. m = 128 with n = 4096); larger sizes return
+ * DSV4_ERR_INVALID_ARGUMENT.  The first call on a device looks up the
+ * array's device address with the device current; make that first call
+ * before any stream capture.  The array is shared by every call in the
+ * process: calls that overlap on the GPU (other streams, other threads)
+ * race on it; serialise them.  Nothing in it needs to start at zero (every
+ * call overwrites the words it reads). */
+DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm_noalloc(const int8_t* a_q, const float* a_scale,
+                                                     int64_t m, int64_t k, const uint8_t* b_mxfp4,
+                                                     const uint8_t* b_shift2, int64_t shift_stride,
+                                                     const float* b_channel_scale, int64_t n,
+                                                     void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
