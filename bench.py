@@ -37,6 +37,11 @@ DECODE_M, PREFILL_M = 64, 8192
 EXP_RANGE = (-8, -4)
 
 
+def _set_experts(e):
+    global E
+    E = e
+
+
 def peaks():
     try:
         d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -61,8 +66,11 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            t0 = time.time()
+            while time.time() - t0 < 10 and (not self.path.exists() or self.path.stat().st_size == 0):
+                time.sleep(0.05)
         except Exception:
             self.proc = None
         return self
@@ -290,12 +298,18 @@ def cpu_reference_sample(steps, warmup, tokens_per_step=1):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=E,
+                    help="number of experts (smaller for ncu captures that must stay a few GB)")
+    ap.add_argument("--only", choices=["decode", "prefill"], default=None,
+                    help="run one workload only (profiling); prints its JSON line")
     args = ap.parse_args()
+    if args.experts != E:
+        _set_experts(args.experts)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -331,11 +345,19 @@ def main():
     tops_i8 = 2.0 * bf16_tf
 
     weights = make_weights(dev, 42)
+    if args.only is not None:
+        m, z = (DECODE_M, None) if args.only == "decode" else (PREFILL_M, 1.1)
+        r = run_workload(weights, m, z, args.steps, args.warmup, dev, rank, world, hbm, tops_i8,
+                         sample_clocks=False)
+        if rank == 0:
+            r.pop("clocks", None)
+            print(json.dumps({"only": args.only, "experts": E, **r}))
+        return
     dec = run_workload(weights, DECODE_M, None, args.steps, args.warmup, dev, rank, world, hbm,
                        tops_i8, sample_clocks=True)
     pre = None
     if not args.no_prefill:
-        pre = run_workload(weights, PREFILL_M, 1.1, max(3, args.steps // 4), args.warmup, dev,
+        pre = run_workload(weights, PREFILL_M, 1.1, max(3, args.steps // 10), args.warmup, dev,
                            rank, world, hbm, tops_i8, sample_clocks=False)
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:

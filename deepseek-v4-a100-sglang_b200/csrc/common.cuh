@@ -3,6 +3,7 @@
 // (TMEM alloc / MMA / commit / load) and the MXFP4 -> INT8 nibble decode.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -27,6 +28,8 @@ enum DeviceErr : int {
   kErrWaitAbFull = 0x103,
   kErrWaitAccFull = 0x104,
   kErrWaitPackedEmpty = 0x105,
+  kErrWaitMeta = 0x106,
+  kErrWaitAccEmpty = 0x107,
 };
 
 // Wait budget: ~2 s of %globaltimer per wait.
@@ -45,6 +48,22 @@ __device__ __forceinline__ void record_error(int code) {
 __device__ __forceinline__ bool device_error_pending() {
   return *reinterpret_cast<volatile int*>(&g_device_status) != 0;
 }
+
+// Optional pipeline timeline (compile with -DDSV4_TRACE; debug builds only):
+// CTA 0 records clock64 at each hand-off of the first kTraceStages stages.
+#ifdef DSV4_TRACE
+constexpr int kTraceStages = 1024;
+constexpr int kTraceEvents = 8;
+__device__ long long g_trace[kTraceEvents][kTraceStages];
+#define DSV4_TRACE_EV(ev, idx)                                                   \
+  do {                                                                           \
+    if (blockIdx.x == 0 && (idx) < kTraceStages) g_trace[ev][idx] = clock64();   \
+  } while (0)
+#else
+#define DSV4_TRACE_EV(ev, idx) \
+  do {                         \
+  } while (0)
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -70,11 +89,29 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// parked (issuing nothing) until the phase completes or ~hint ns pass, so
+// waiting warps do not steal issue slots from the decode warps.
+constexpr uint32_t kWaitSuspendHintNs = 100000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kWaitSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking probe of a phase.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -89,7 +126,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
   unsigned long long t0 = globaltimer_ns();
   uint32_t n = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++n & 255u) == 0) {
+    if ((++n & 7u) == 0) {
       if (device_error_pending()) return false;
       if (globaltimer_ns() - t0 > kWaitBudgetNs) {
         record_error(code);
@@ -123,6 +160,43 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// Tiled tensor-map (TMA) loads, no multicast, completion on an mbarrier.
+// The shared-memory destination must be 128-byte aligned.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// Row gather: 4 rows (arbitrary row coordinates, out-of-range -> zeros) of a
+// 2-D tensor map whose box is 1 row high, written as 4 consecutive box rows.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int r0,
+                                            int r1, int r2, int r3, uint32_t bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -185,6 +259,32 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M=128 lanes x K int8, K-major,
+// 4 int8 per 32-bit column) read from tensor memory.
+__device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 bits, 16 consecutive columns per thread, registers -> TMEM.
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Arrive on `bar` once all tcgen05.mma issued so far by this thread complete.

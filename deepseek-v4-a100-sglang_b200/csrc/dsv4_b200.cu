@@ -1,6 +1,8 @@
 // C ABI of the B200 MXFP4/INT8 MoE path (declared in include/dsv4_b200.h).
 // Single translation unit: the device status word and every kernel live here.
 
+#include <cudaTypedefs.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -44,10 +46,8 @@ int g_sm_count[kMaxDevices] = {};
 
 template <int TN, int EPI>
 struct GemmKernel {
-  static constexpr int kDW = TN <= 64 ? 4 : 8;
-  static constexpr int kThreads = (4 + kDW) * 32;
   static constexpr int kSmem = TcGemmCfg<TN>::kSmemLaunch;
-  static void* fn() { return reinterpret_cast<void*>(&mxfp4_int8_tc_gemm_kernel<TN, EPI, kDW>); }
+  static void* fn() { return reinterpret_cast<void*>(&mxfp4_int8_tc_gemm_kernel<TN, EPI>); }
 };
 
 template <int EPI>
@@ -61,7 +61,6 @@ cudaError_t set_attrs_epi() {
   one(GemmKernel<32, EPI>::fn(), GemmKernel<32, EPI>::kSmem);
   one(GemmKernel<64, EPI>::fn(), GemmKernel<64, EPI>::kSmem);
   one(GemmKernel<128, EPI>::fn(), GemmKernel<128, EPI>::kSmem);
-  one(GemmKernel<256, EPI>::fn(), GemmKernel<256, EPI>::kSmem);
   return e;
 }
 
@@ -101,24 +100,95 @@ int sm_count() {
   return g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
 }
 
+// Persistent launch: one CTA per SM (never more CTAs than work items).
 template <int EPI>
-int launch_gemm(int tn, dim3 grid, const TcGemmParams& p, cudaStream_t st) {
+int launch_gemm(int tn, int64_t max_items, const TcGemmParams& p, cudaStream_t st) {
+  const int64_t ctas = max_items < sm_count() ? max_items : sm_count();
+  if (ctas <= 0) return DSV4_OK;
+  const dim3 grid(static_cast<unsigned>(ctas));
   switch (tn) {
-#define DSV4_CASE(T)                                                                     \
-  case T:                                                                                \
-    mxfp4_int8_tc_gemm_kernel<T, EPI, GemmKernel<T, EPI>::kDW>                           \
-        <<<grid, GemmKernel<T, EPI>::kThreads, GemmKernel<T, EPI>::kSmem, st>>>(p);      \
+#define DSV4_CASE(T)                                                                    \
+  case T:                                                                               \
+    mxfp4_int8_tc_gemm_kernel<T, EPI><<<grid, kGemmThreads, GemmKernel<T, EPI>::kSmem, st>>>(p); \
     break;
     DSV4_CASE(16)
     DSV4_CASE(32)
     DSV4_CASE(64)
     DSV4_CASE(128)
-    DSV4_CASE(256)
 #undef DSV4_CASE
     default:
       return fail(DSV4_ERR_INVALID_ARGUMENT, "unsupported token tile %d", tn);
   }
   return check_launch("mxfp4_int8_tc_gemm_kernel");
+}
+
+// ---- tensor maps for the weight stream (driver entry point, no -lcuda) ----
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// b_mxfp4 [E][KB][NG8][128] as 3-D {128, NG8, E*KB}; b_shift2 [E][SS][NG8][8]
+// as 2-D {NG8*8, E*SS}.  Box rows = 128 (plain) or 64 (SwiGLU halves).
+int encode_weight_maps(TcGemmParams& p, const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                       int64_t experts, int64_t kb, int64_t ss, int64_t ng8, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(b_mxfp4) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(b_shift2) & 15) == 0,
+               "weight tensors must be 16-byte aligned");
+  DSV4_REQUIRE(experts * kb < (1ll << 31) && experts * ss < (1ll << 31), "weight too large");
+  {
+    cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(ng8), static_cast<cuuint64_t>(experts * kb)};
+    cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(ng8 * 128)};
+    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(box_rows / 8), 8};  // 256 K per stage
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(&p.map_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(b_mxfp4),
+                     dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (packed) encode failed: %d", (int)r);
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(ng8 * 8), static_cast<cuuint64_t>(experts * ss)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ng8 * 8)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_rows), 2};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&p.map_shift, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(b_shift2),
+                     dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (shift) encode failed: %d", (int)r);
+  }
+  p.kb_per_expert = static_cast<int>(kb);
+  p.ss_per_expert = static_cast<int>(ss);
+  return DSV4_OK;
+}
+
+// activations int8 [rows][k] (row stride k) as 2-D {k, rows}, box {128, 1},
+// 128-byte swizzle (the K-major SW128 layout of the MMA B operand).
+int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, "a_q must be 16-byte aligned");
+  DSV4_REQUIRE(rows >= 1 && rows < (1ll << 31), "bad activation row count");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
+  cuuint32_t box[2] = {128, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&p.map_act, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(a), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (activations) encode failed: %d", (int)r);
+  return DSV4_OK;
 }
 
 int64_t align_capacity(int64_t numel, int64_t experts, int64_t bm) {
@@ -169,16 +239,13 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   p.a_scale = a_scale;
   p.lda = k;
   p.a_rows = m_in;
-  p.b_packed = b_mxfp4;
-  p.b_shift = b_shift2;
   p.cs = cs;
-  p.ng8 = static_cast<int>(n_rows / 8);
-  p.b_expert_stride = (k / 32) * p.ng8 * 128;
-  p.s_expert_stride = shift_stride * p.ng8 * 8;
   p.n = static_cast<int>(n_rows);
   p.inter = static_cast<int>(inter);
-  p.k_stages = static_cast<int>(k / 128);
+  p.k_stages = static_cast<int>((k / 32 + 7) / 8);  // 256-K stages
   p.stages_per_split = p.k_stages;
+  p.splits = 1;
+  p.row_tiles = static_cast<int>(tile_rows_y);
   p.moe = 1;
   p.sorted_ids = sorted_ids;
   p.expert_ids = expert_ids;
@@ -191,17 +258,21 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   p.ldo = ldo;
   p.has_clamp = has_clamp;
   p.clamp_limit = clamp_limit;
-  dim3 grid(static_cast<unsigned>(grid_m), static_cast<unsigned>(tile_rows_y), 1);
-  if (epi == kEpiSwiglu) return launch_gemm<kEpiSwiglu>(static_cast<int>(block_m), grid, p, as_stream(stream));
-  return launch_gemm<kEpiBf16>(static_cast<int>(block_m), grid, p, as_stream(stream));
+  if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, experts, k / 32, shift_stride, n_rows / 8,
+                                 epi == kEpiSwiglu ? 64 : 128))
+    return r;
+  if (int r = encode_act_map(p, a_q, m_in, k)) return r;
+  const int64_t max_items = grid_m * tile_rows_y;
+  if (epi == kEpiSwiglu)
+    return launch_gemm<kEpiSwiglu>(static_cast<int>(block_m), max_items, p, as_stream(stream));
+  return launch_gemm<kEpiBf16>(static_cast<int>(block_m), max_items, p, as_stream(stream));
 }
 
 int dense_tile(int64_t m) {
   if (m <= 16) return 16;
   if (m <= 32) return 32;
   if (m <= 64) return 64;
-  if (m <= 128) return 128;
-  return 256;
+  return 128;
 }
 
 int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
@@ -214,27 +285,26 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   p.a_scale = a_scale;
   p.lda = k;
   p.a_rows = m;
-  p.b_packed = b_mxfp4;
-  p.b_shift = b_shift2;
   p.cs = cs;
-  p.ng8 = static_cast<int>(n / 8);
-  p.b_expert_stride = 0;
-  p.s_expert_stride = 0;
   p.n = static_cast<int>(n);
-  p.k_stages = static_cast<int>(k / 128);
+  p.k_stages = static_cast<int>((k / 32 + 7) / 8);  // 256-K stages
   p.stages_per_split = static_cast<int>((p.k_stages + splits - 1) / splits);
+  p.splits = static_cast<int>((p.k_stages + p.stages_per_split - 1) / p.stages_per_split);
   p.moe = 0;
   p.m = static_cast<int>(m);
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.out_i32 = out_i32;
   p.ldo = ld;
   p.split_stride = split_stride;
+  if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, 1, k / 32, shift_stride, n / 8, 128))
+    return r;
+  if (int r = encode_act_map(p, a_q, m, k)) return r;
   const int tn = dense_tile(m);
-  const int64_t gz = (p.k_stages + p.stages_per_split - 1) / p.stages_per_split;
-  dim3 grid(static_cast<unsigned>((m + tn - 1) / tn), static_cast<unsigned>(n / 128),
-            static_cast<unsigned>(gz));
-  if (epi == kEpiI32) return launch_gemm<kEpiI32>(tn, grid, p, as_stream(stream));
-  return launch_gemm<kEpiBf16>(tn, grid, p, as_stream(stream));
+  p.m_tiles = static_cast<int>((m + tn - 1) / tn);
+  p.row_tiles = static_cast<int>(n / 128);
+  const int64_t max_items = static_cast<int64_t>(p.m_tiles) * p.row_tiles * p.splits;
+  if (epi == kEpiI32) return launch_gemm<kEpiI32>(tn, max_items, p, as_stream(stream));
+  return launch_gemm<kEpiBf16>(tn, max_items, p, as_stream(stream));
 }
 
 // Fixed split-K workspace of dsv4_b200_mxfp4_int8_dense_gemm_noalloc:
@@ -454,7 +524,7 @@ int dsv4_b200_mxfp4_int8_dense_gemm(const int8_t* a_q, const float* a_scale, int
   DSV4_REQUIRE(a_q && a_scale && b_mxfp4 && b_shift2 && b_channel_scale && out,
                "null pointer argument");
   DSV4_REQUIRE(m <= 0x7FFFFFFF, "m too large");
-  const int64_t k_stages = k / 128;
+  const int64_t k_stages = (k / 32 + 7) / 8;  // 256-K stages of the GEMM kernel
   int64_t splits = 1;
   if (partial != nullptr && m <= 128 && partial_splits >= 2 && k_stages >= 2) {
     DSV4_REQUIRE(partial_ld >= n, "partial leading dimension %lld < N %lld",
@@ -518,5 +588,16 @@ int dsv4_b200_mxfp4_int8_dense_gemm_noalloc(const int8_t* a_q, const float* a_sc
   return dsv4_b200_mxfp4_int8_dense_gemm(a_q, a_scale, m, k, b_mxfp4, b_shift2, shift_stride,
                                          b_channel_scale, n, out, scratch, splits, ld, stream);
 }
+
+#ifdef DSV4_TRACE
+DSV4_API int dsv4_b200_debug_trace(long long* host, int reset) {
+  cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace));
+  if (reset) {
+    static long long zeros[kTraceEvents][kTraceStages];
+    cudaMemcpyToSymbol(g_trace, zeros, sizeof(g_trace));
+  }
+  return DSV4_OK;
+}
+#endif
 
 }  // extern "C"

@@ -1,24 +1,39 @@
 // MXFP4-weight x INT8-activation GEMM on the 5th-generation tensor core.
 //
-// One kernel serves the dense GEMM (reference DENSE_ENTRY:334-433), the
-// grouped MoE GEMMs W13 / W2 (reference MOE_ENTRY:146-272, MOE_CORE:380-646)
-// and the W13 GEMM with a fused SwiGLU epilogue (reference PYMOE:916-935).
+// One persistent kernel serves the dense GEMM (reference
+// DENSE_ENTRY:334-433), the grouped MoE GEMMs W13 / W2 (reference
+// MOE_ENTRY:146-272, MOE_CORE:380-646) and the W13 GEMM with a fused SwiGLU
+// epilogue (reference PYMOE:916-935).
 //
 // Orientation ("swap-AB"): the decoded weight tile is the MMA A operand
-// (M = 128 weight rows = output channels), the gathered token rows are the
-// B operand (N = 16..256 tokens), K-major both, int32 accumulators in TMEM
-// laid out [channel lane][token column].  One weight tile, once decoded,
-// serves every token of the tile.
+// (M = 128 weight rows = output channels) and lives in tensor memory; the
+// gathered token rows are the B operand (N = 16..128 tokens, SW128 K-major
+// in shared memory); int32 accumulators in TMEM, [channel lane][token col].
+// One weight tile, once decoded, serves every token of the tile.
 //
-// Warp roles (block = (4 + DECODE_WARPS) warps):
-//   warp 0         bulk-copy producer: packed FP4 codes + 2-bit shifts of the
-//                  weight tile, 128 K per stage, into the packed ring
-//   warp 1         TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 2..3     activation gather (cp.async, 16 B, zero-fill) into the
-//                  SW128 K-major B ring
-//   warps 4..      FP4 -> INT8 decode from the packed ring into the SW128
-//                  K-major A ring; afterwards the epilogue (TMEM -> regs ->
-//                  scales -> bf16 / int32 / SwiGLU -> global)
+// Work items: (token block b, weight row tile y, K split z).  One CTA per SM
+// walks items blockIdx.x, blockIdx.x + gridDim.x, ...; every role walks the
+// same sequence, so the weight stream never drains between items.
+//
+// Issue cost shapes the design: in the issuing thread one tcgen05.mma costs
+// ~64 cycles, one mbarrier wait ~245 cycles (even when already complete) and
+// one commit ~50.  So each 128-K stage has ONE ready barrier (decoded A and
+// gathered B together) and ONE commit, and two issuer warps take alternate
+// stages of an item into two accumulators (int32 sums are exact; the
+// epilogue adds them), which halves the per-stage issue time per SM.
+//
+// Warp roles (21 warps):
+//   warp 0       TMA producer: packed FP4 codes (3-D tensor map) + 2-bit
+//                shifts (2-D tensor map), 128 K per stage, deep packed ring
+//   warp 1       TMEM allocator; MMA issuer for even stages of each item
+//   warps 2..3   per-item token metadata; warp 2 lane 0 gathers the token
+//                rows with TMA tile::gather4 into the SW128 K-major B ring
+//   warps 4..7   epilogue: TMEM -> registers -> scales -> bf16 / int32 /
+//                SwiGLU -> global (overlaps the next item's main loop)
+//   warps 8..19  FP4 -> INT8 decode from the packed ring straight into TMEM
+//                (tcgen05.st), three groups of 4 warps taking stages in turn:
+//                one 64-column A slot per 128x256 stage
+//   warp 20      MMA issuer for odd stages of each item
 #pragma once
 
 #include "common.cuh"
@@ -28,25 +43,32 @@ namespace dsv4 {
 enum Epilogue : int { kEpiBf16 = 0, kEpiI32 = 1, kEpiSwiglu = 2 };
 
 struct TcGemmParams {
+  // Weight tensor maps (uint8):
+  //   map_packed  3-D {128 B, NG8 groups, E*KB}: box {128, 16 (8 for SwiGLU), 4}
+  //   map_shift   2-D {NG8*8 B, E*SS}:           box {128 (64 for SwiGLU), 1}
+  CUtensorMap map_packed;
+  CUtensorMap map_shift;
+  // activations int8 [a_rows][lda] as 2-D {K, a_rows}, box {128 B, 1 row},
+  // 128-byte swizzle: rows are gathered 4 at a time (tile::gather4)
+  CUtensorMap map_act;
+  int kb_per_expert;        // KB = K / 32
+  int ss_per_expert;        // shift stride SS
   // activations
   const int8_t* a;
   const float* a_scale;
   int64_t lda;
   int64_t a_rows;
-  // weights in the repacked layout
-  const uint8_t* b_packed;  // [E][KB][NG8][128]
-  const uint8_t* b_shift;   // [E][SS][NG8][8]
   const float* cs;          // [E][N]
-  int64_t b_expert_stride;  // bytes per expert in b_packed
-  int64_t s_expert_stride;  // bytes per expert in b_shift
   int n;                    // weight rows (output channels) per expert
-  int ng8;                  // ceil(n / 8)
   int inter;                // SwiGLU: intermediate size (gate rows [0,I), up rows [I,2I))
   int k_stages;             // K / 128
   int stages_per_split;
+  int splits;
+  int row_tiles;            // weight row tiles per expert
   // token rows of each tile
   int moe;                  // 0: dense rows, 1: rows from the aligned permutation
   int m;                    // dense: number of rows
+  int m_tiles;              // dense: number of token tiles
   const int32_t* sorted_ids;
   const int32_t* expert_ids;
   const int32_t* ntpp;      // num_tokens_post_padded[0]
@@ -63,334 +85,505 @@ struct TcGemmParams {
   int has_clamp;
 };
 
+constexpr int kDecodeGroups = 3;                    // groups of 4 warps, alternate stages
+constexpr int kDecodeWarps = 4 * kDecodeGroups;
+constexpr int kIssuer1Warp = 8 + kDecodeWarps;       // second MMA issuer
+constexpr int kGemmWarps = kIssuer1Warp + 1;
+constexpr int kGemmThreads = kGemmWarps * 32;
+constexpr int kIssuers = 2;
+
 template <int TN>
 struct TcGemmCfg {
-  static constexpr int kStagesAB = 3;
-  static constexpr int kStagesP = 4;
-  static constexpr int kABytes = 128 * 128;     // 128 weight rows x 128 K (int8)
-  static constexpr int kBBytes = TN * 128;      // TN token rows x 128 K (int8)
-  static constexpr int kPBytes = 128 * 128 / 2; // packed FP4 codes of one stage
-  static constexpr int kShBytes = 128;
-  static constexpr int kOffA = 0;
-  static constexpr int kOffB = kOffA + kStagesAB * kABytes;
-  static constexpr int kOffP = kOffB + kStagesAB * kBBytes;
+  static constexpr int kBHalf = TN * 128;        // one 128-K SW128 sub-tile of B
+  static constexpr int kBBytes = 2 * kBHalf;     // TN token rows x 256 K (int8)
+  static constexpr int kPBytes = 128 * 256 / 2;  // packed FP4 codes of one 256-K stage
+  // shift slot per stage: [2 x 128 B] (plain) or gate [2 x 64 B] at +0 and up
+  // [2 x 64 B] at +128 (SwiGLU); tiled TMA destinations must be 128-byte aligned
+  static constexpr int kShBytes = 256;
+  // TMEM (512 columns): [issuer accumulators x slots], then 64-column A slots
+  static constexpr int kAccCols = TN < 32 ? 32 : TN;
+  static constexpr int kAccSlots = TN <= 64 ? 2 : 1;
+  static constexpr int kAColBase = kIssuers * kAccSlots * kAccCols;
+  static constexpr int kStagesRaw = (512 - kAColBase) / 64;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;  // A (TMEM) + B (smem) ring
+  static constexpr int kTmemCols = 512;
+  static constexpr int kStgBytes = 16 * 128 * 2;   // SwiGLU staging (16 cols x 128 rows bf16)
+  static constexpr int kMetaBytes = TN * 12 + 16;  // src, orow, ascale, per-warp last
+  static constexpr int kFixed = kStages * kBBytes + kStgBytes + 2 * kMetaBytes + 1024;
+  static constexpr int kBudget = 227 * 1024 - 1024;  // minus alignment slack
+  static constexpr int kStagesPRaw = (kBudget - kFixed) / (kPBytes + kShBytes);
+  static constexpr int kStagesP = kStagesPRaw > 16 ? 16 : kStagesPRaw;
+  static constexpr int kOffB = 0;
+  static constexpr int kOffP = kOffB + kStages * kBBytes;
   static constexpr int kOffSh = kOffP + kStagesP * kPBytes;
-  static constexpr int kOffBar = kOffSh + kStagesP * kShBytes;
-  static constexpr int kNumBars = 2 * kStagesP + 2 * kStagesAB + 1;
-  static constexpr int kOffMeta = kOffBar + kNumBars * 8;
-  static constexpr int kOffSrc = kOffMeta;
-  static constexpr int kOffOrow = kOffSrc + TN * 4;
-  static constexpr int kOffAsc = kOffOrow + TN * 4;
-  static constexpr int kOffMisc = kOffAsc + TN * 4;  // tmem addr, last valid column
+  static constexpr int kOffStg = kOffSh + kStagesP * kShBytes;
+  static constexpr int kOffMeta = kOffStg + kStgBytes;
+  static constexpr int kOffBar = kOffMeta + 2 * kMetaBytes;
+  // barriers: pk_full/empty[SP], ab_full/empty[S], acc_full/empty[2], meta_full/empty[2]
+  static constexpr int kNumBars = 2 * kStagesP + 2 * kStages + 8;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
-  static constexpr int kTmemCols = TN < 32 ? 32 : TN;
-  static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "token tile");
-  static_assert(kStagesAB * kABytes % 1024 == 0 && kBBytes % 1024 == 0, "alignment");
+  static_assert(TN % 16 == 0 && TN >= 16 && TN <= 128, "token tile");
+  static_assert(kStagesP >= 3 && kStages >= 4, "rings too shallow");
+  static_assert(kSmemLaunch <= 227 * 1024, "shared memory budget");
+  static_assert(kBHalf % 1024 == 0 && kOffMeta % 16 == 0 && kOffBar % 8 == 0, "alignment");
 };
 
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 
-template <int TN, int EPI, int DW>
-__global__ void __launch_bounds__((4 + DW) * 32, DW == 4 ? 2 : 1)
-mxfp4_int8_tc_gemm_kernel(const TcGemmParams p) {
+struct Item {
+  int b, y, z;
+  int expert;
+  bool valid;
+};
+
+__device__ __forceinline__ Item get_item(const TcGemmParams& p, int i, int n_blocks) {
+  Item it;
+  if (p.moe) {
+    it.z = 0;
+    it.b = i % n_blocks;
+    it.y = i / n_blocks;
+    it.expert = __ldg(p.expert_ids + it.b);
+    it.valid = it.expert >= 0;
+  } else {
+    it.z = i % p.splits;
+    const int r = i / p.splits;
+    it.b = r % p.m_tiles;
+    it.y = r / p.m_tiles;
+    it.expert = 0;
+    it.valid = true;
+  }
+  return it;
+}
+
+template <int TN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   using C = TcGemmCfg<TN>;
-  constexpr int S = C::kStagesAB;
+  constexpr int S = C::kStages;
   constexpr int SP = C::kStagesP;
-  constexpr int kThreads = (4 + DW) * 32;
-  static_assert(DW == 4 || DW == 8, "decode warps");
+  constexpr int AS = C::kAccSlots;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  // ---- tile coordinates (uniform exits before any barrier / TMEM use) ----
-  const int tile_x = blockIdx.x;
-  const int tile_y = blockIdx.y;
-  int expert = 0;
+  // ---- the item space (identical in every thread) ----
+  int n_blocks, n_items;
   if (p.moe) {
-    if (tile_x * p.block_m >= __ldg(p.ntpp)) return;
-    expert = __ldg(p.expert_ids + tile_x);
-    if (expert < 0) return;
+    n_blocks = __ldg(p.ntpp) / p.block_m;
+    n_items = n_blocks * p.row_tiles;
+  } else {
+    n_blocks = p.m_tiles;
+    n_items = p.m_tiles * p.row_tiles * p.splits;
   }
-  const int ks_begin = blockIdx.z * p.stages_per_split;
-  const int ks_end = min(p.k_stages, ks_begin + p.stages_per_split);
-  const int nks = ks_end - ks_begin;
-  if (nks <= 0) return;
+  if (static_cast<int>(blockIdx.x) >= n_items) return;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t bar0 = smem_u32(smem + C::kOffBar);
   auto pk_full = [&](int s) { return bar0 + 8u * s; };
   auto pk_empty = [&](int s) { return bar0 + 8u * (SP + s); };
   auto ab_full = [&](int s) { return bar0 + 8u * (2 * SP + s); };
   auto ab_empty = [&](int s) { return bar0 + 8u * (2 * SP + S + s); };
-  const uint32_t acc_full = bar0 + 8u * (2 * SP + 2 * S);
-  int* s_src = reinterpret_cast<int*>(smem + C::kOffSrc);
-  int* s_orow = reinterpret_cast<int*>(smem + C::kOffOrow);
-  float* s_asc = reinterpret_cast<float*>(smem + C::kOffAsc);
+  constexpr int kX = 2 * SP + 2 * S;
+  auto acc_full = [&](int s) { return bar0 + 8u * (kX + s); };
+  auto acc_empty = [&](int s) { return bar0 + 8u * (kX + 2 + s); };
+  auto meta_full = [&](int s) { return bar0 + 8u * (kX + 4 + s); };
+  auto meta_empty = [&](int s) { return bar0 + 8u * (kX + 6 + s); };
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
-  int* s_last = reinterpret_cast<int*>(smem + C::kOffMisc + 4);
+  auto meta_src = [&](int s) {
+    return reinterpret_cast<int*>(smem + C::kOffMeta + s * C::kMetaBytes);
+  };
+  auto meta_orow = [&](int s) { return meta_src(s) + TN; };
+  auto meta_asc = [&](int s) { return reinterpret_cast<float*>(meta_src(s) + 2 * TN); };
+  auto meta_last = [&](int s) { return meta_src(s) + 3 * TN; };  // [2] per gather warp
 
   if (tid == 0) {
     for (int s = 0; s < SP; ++s) {
       mbar_init(pk_full(s), 1);
-      mbar_init(pk_empty(s), DW);
+      mbar_init(pk_empty(s), 4);
     }
     for (int s = 0; s < S; ++s) {
-      mbar_init(ab_full(s), DW + 2);
+      mbar_init(ab_full(s), 4 + 1);
       mbar_init(ab_empty(s), 1);
     }
-    mbar_init(acc_full, 1);
-    *s_last = -1;
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(acc_full(s), kIssuers);
+      mbar_init(acc_empty(s), 4);
+      mbar_init(meta_full(s), 2);
+      mbar_init(meta_empty(s), 4);
+    }
     mbar_fence_init();
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(s_tmem), C::kTmemCols);
     tmem_relinquish();
   }
-  __syncthreads();
-
-  // ---- token rows of this tile ----
-  for (int j = tid; j < TN; j += kThreads) {
-    int src = -1, orow = -1;
-    float asc = 0.f;
-    if (p.moe) {
-      const int pos = tile_x * p.block_m + j;
-      if (j < p.block_m) {
-        const int slot = __ldg(p.sorted_ids + pos);
-        if (slot >= 0 && slot < p.num_valid) {
-          src = p.src_is_slot ? slot : slot / p.topk;
-          orow = slot;
-        }
-      }
-    } else {
-      const int m = tile_x * TN + j;
-      if (m < p.m) {
-        src = m;
-        orow = m;
-      }
-    }
-    if (src >= p.a_rows) src = -1, orow = -1;
-    if (src >= 0) {
-      asc = p.a_scale != nullptr ? __ldg(p.a_scale + src) : 0.f;
-      atomicMax(s_last, j);
-    }
-    s_src[j] = src;
-    s_orow[j] = orow;
-    s_asc[j] = asc;
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  const int last = *s_last;
-  const int n_mma = ((last + 16) / 16) * 16;  // columns the MMA computes (>= 16)
 
-  if (last >= 0) {
-    // weight row groups of this tile
-    int g0, g1;
-    if (EPI == kEpiSwiglu) {
-      g0 = (tile_y * 64) >> 3;             // gate rows j0 .. j0+63
-      g1 = (p.inter + tile_y * 64) >> 3;   // up rows I+j0 .. I+j0+63
-    } else {
-      g0 = tile_y * 16;                    // rows 128*tile_y ..
-      g1 = g0 + 8;
-    }
-    const uint8_t* bp = p.b_packed + static_cast<int64_t>(expert) * p.b_expert_stride;
-    const uint8_t* bs = p.b_shift + static_cast<int64_t>(expert) * p.s_expert_stride;
+  // stages are 256 K (8 blocks of 32); the last one of K may be 128 K
+  auto k_range = [&](const Item& it, int& ks0, int& nks) {
+    ks0 = it.z * p.stages_per_split;
+    nks = min(p.k_stages, ks0 + p.stages_per_split) - ks0;
+  };
+  auto stage_kb = [&](int ks) { return min(8, p.kb_per_expert - ks * 8); };
+  auto n_mma_of = [&](int ms) {
+    const int* lw = meta_last(ms);
+    const int last = max(lw[0], lw[1]);
+    return ((max(last, 0) + 16) / 16) * 16;
+  };
 
-    if (warp == 0) {
-      // ------------------------- bulk-copy producer -------------------------
-      if (lane == 0) {
-        const uint64_t pol = l2_policy_evict_first();
-        for (int it = 0; it < nks; ++it) {
-          const int sp = it % SP;
-          const uint32_t ph = (it / SP) & 1;
-          mbar_wait(pk_empty(sp), ph ^ 1, kErrWaitPackedEmpty);
-          mbar_arrive_expect_tx(pk_full(sp), C::kPBytes + C::kShBytes);
-          const int ks = ks_begin + it;
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&p.map_packed);
+      tma_prefetch_desc(&p.map_shift);
+      const uint64_t pol = l2_policy_evict_first();
+      uint32_t g = 0;
+      for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+        const Item it = get_item(p, i, n_blocks);
+        if (!it.valid) continue;
+        int ks0, nks;
+        k_range(it, ks0, nks);
+        int g0, g1;
+        if (EPI == kEpiSwiglu) {
+          g0 = (it.y * 64) >> 3;            // gate rows j0 .. j0+63
+          g1 = (p.inter + it.y * 64) >> 3;  // up rows I+j0 .. I+j0+63
+        } else {
+          g0 = it.y * 16;                   // rows 128*y .. 128*y+127
+          g1 = g0;
+        }
+        for (int s = 0; s < nks; ++s, ++g) {
+          const int sp = g % SP;
+          mbar_wait(pk_empty(sp), ((g / SP) & 1) ^ 1, kErrWaitPackedEmpty);
+          DSV4_TRACE_EV(0, g);
+          mbar_arrive_expect_tx(pk_full(sp), C::kPBytes + 256);
+          const int ks = ks0 + s;
           const uint32_t dstp = smem_u32(smem + C::kOffP + sp * C::kPBytes);
-          for (int kb = 0; kb < 4; ++kb) {
-            const int64_t kbg = static_cast<int64_t>(ks) * 4 + kb;
-            const uint8_t* src0 = bp + (kbg * p.ng8 + g0) * 128;
-            const uint8_t* src1 = bp + (kbg * p.ng8 + g1) * 128;
-            bulk_g2s(dstp + kb * 2048, src0, 1024, pk_full(sp), pol);
-            bulk_g2s(dstp + kb * 2048 + 1024, src1, 1024, pk_full(sp), pol);
-          }
           const uint32_t dsts = smem_u32(smem + C::kOffSh + sp * C::kShBytes);
-          bulk_g2s(dsts, bs + (static_cast<int64_t>(ks) * p.ng8 + g0) * 8, 64, pk_full(sp), pol);
-          bulk_g2s(dsts + 64, bs + (static_cast<int64_t>(ks) * p.ng8 + g1) * 8, 64, pk_full(sp),
-                   pol);
+          const int kb_row = it.expert * p.kb_per_expert + ks * 8;
+          const int sh_row = it.expert * p.ss_per_expert + ks * 2;
+          if (EPI == kEpiSwiglu) {
+            // smem: [gate|up][kb 0..7][8 groups][128 B]; shifts gate [2][64] @0, up @128
+            tma_load_3d(dstp, &p.map_packed, 0, g0, kb_row, pk_full(sp), pol);
+            tma_load_3d(dstp + 8192, &p.map_packed, 0, g1, kb_row, pk_full(sp), pol);
+            tma_load_2d(dsts, &p.map_shift, g0 * 8, sh_row, pk_full(sp), pol);
+            tma_load_2d(dsts + 128, &p.map_shift, g1 * 8, sh_row, pk_full(sp), pol);
+          } else {
+            // smem: [kb 0..7][16 groups][128 B]; shifts [2][128]
+            tma_load_3d(dstp, &p.map_packed, 0, g0, kb_row, pk_full(sp), pol);
+            tma_load_2d(dsts, &p.map_shift, g0 * 8, sh_row, pk_full(sp), pol);
+          }
         }
       }
-    } else if (warp == 1) {
-      // ----------------------------- MMA issuer -----------------------------
-      if (lane == 0) {
-        const uint32_t idesc = idesc_i8(128, n_mma);
-        for (int it = 0; it < nks; ++it) {
-          const int sa = it % S;
-          const uint32_t ph = (it / S) & 1;
-          mbar_wait(ab_full(sa), ph, kErrWaitAbFull);
+    }
+  } else if (warp == 1 || warp == kIssuer1Warp) {
+    // ------------------------------- MMA issuers -------------------------------
+    if (lane == 0) {
+      const int j = warp == 1 ? 0 : 1;  // this issuer takes stages s = j, j+2, ...
+      uint32_t g = 0, t = 0;
+      const uint64_t bdesc0 = smem_desc_sw128(smem_u32(smem + C::kOffB));
+      for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+        const Item it = get_item(p, i, n_blocks);
+        if (!it.valid) continue;
+        int ks0, nks;
+        k_range(it, ks0, nks);
+        const int ms = t & 1;
+        const int as = t % AS;
+        mbar_wait(meta_full(ms), (t >> 1) & 1, kErrWaitMeta);
+        const uint32_t idesc = idesc_i8(128, n_mma_of(ms));
+        mbar_wait(acc_empty(as), ((t / AS) & 1) ^ 1, kErrWaitAccEmpty);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (as * kIssuers + j) * C::kAccCols;
+        for (int s = j; s < nks; s += 2) {
+          const uint32_t gs = g + s;
+          const int sa = gs % S;
+          mbar_wait(ab_full(sa), (gs / S) & 1, kErrWaitAbFull);
+          DSV4_TRACE_EV(3, gs);
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + C::kOffA + sa * C::kABytes);
-          const uint32_t b_base = smem_u32(smem + C::kOffB + sa * C::kBBytes);
+          const uint32_t a_tmem = tmem + C::kAColBase + sa * 64;
+          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((sa * C::kBBytes) >> 4);
+          const int nkb = stage_kb(ks0 + s);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            mma_i8(tmem, smem_desc_sw128(a_base + kk * 32), smem_desc_sw128(b_base + kk * 32),
-                   idesc, (it > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk) {
+            if (kk < nkb)
+              mma_i8_ts(d_tmem, a_tmem + kk * 8,
+                        bdesc + static_cast<uint64_t>(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4),
+                        idesc, (s > j || kk > 0) ? 1u : 0u);
           }
           mma_commit(ab_empty(sa));
+          DSV4_TRACE_EV(6, gs);
         }
-        mma_commit(acc_full);
+        mma_commit(acc_full(as));
+        g += nks;
+        ++t;
       }
-    } else if (warp < 4) {
-      // -------------------------- activation gather -------------------------
-      const int gt = tid - 64;
-      constexpr int LAG = 1;
-      for (int it = 0; it < nks; ++it) {
-        const int sa = it % S;
-        const uint32_t ph = (it / S) & 1;
-        mbar_wait(ab_empty(sa), ph ^ 1, kErrWaitAbEmpty);
-        const int64_t k0 = static_cast<int64_t>(ks_begin + it) * 128;
-        const uint32_t b_base = smem_u32(smem + C::kOffB + sa * C::kBBytes);
-        for (int idx = gt; idx < n_mma * 8; idx += 64) {
-          const int j = idx >> 3;
-          const int c = idx & 7;
-          const int src = s_src[j];
-          const uint32_t dst = b_base + (j >> 3) * 1024 + (j & 7) * 128 + ((c ^ (j & 7)) << 4);
-          const int8_t* g = src >= 0 ? p.a + static_cast<int64_t>(src) * p.lda + k0 + c * 16 : p.a;
-          cp_async_16(dst, g, src >= 0 ? 16u : 0u);
+    }
+  } else if (warp < 4) {
+    // ------------------- token metadata + activation gather -------------------
+    const int gt = tid - 64;
+    uint32_t g = 0, t = 0;
+    const uint64_t pol = l2_policy_evict_last();  // token rows are re-read by every row tile
+    if (gt == 0) tma_prefetch_desc(&p.map_act);
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+      const Item it = get_item(p, i, n_blocks);
+      if (!it.valid) continue;
+      int ks0, nks;
+      k_range(it, ks0, nks);
+      const int ms = t & 1;
+      mbar_wait(meta_empty(ms), ((t >> 1) & 1) ^ 1, kErrWaitMeta);
+      int* src_s = meta_src(ms);
+      int* orow_s = meta_orow(ms);
+      float* asc_s = meta_asc(ms);
+      int my_last = -1;
+      for (int jj = gt; jj < TN; jj += 64) {
+        int src = -1, orow = -1;
+        float asc = 0.f;
+        if (p.moe) {
+          if (jj < p.block_m) {
+            const int slot = __ldg(p.sorted_ids + it.b * p.block_m + jj);
+            if (slot >= 0 && slot < p.num_valid) {
+              src = p.src_is_slot ? slot : slot / p.topk;
+              orow = slot;
+            }
+          }
+        } else {
+          const int m = it.b * TN + jj;
+          if (m < p.m) src = orow = m;
         }
-        cp_async_commit();
-        if (it >= LAG) {
-          cp_async_wait<LAG>();
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(ab_full((it - LAG) % S));
+        if (src >= p.a_rows) src = -1, orow = -1;
+        if (src >= 0) {
+          asc = p.a_scale != nullptr ? __ldg(p.a_scale + src) : 0.f;
+          my_last = jj;
         }
+        src_s[jj] = src;
+        orow_s[jj] = orow;
+        asc_s[jj] = asc;
       }
-      cp_async_wait<0>();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        for (int it = (nks > LAG ? nks - LAG : 0); it < nks; ++it) mbar_arrive(ab_full(it % S));
-      }
-    } else {
-      // ------------------------ FP4 -> INT8 decode -------------------------
-      const int d = tid - 128;
-      const int row = d & 127;
-      constexpr int kKbPerThread = 16 / DW;  // 4 (DW=4) or 2 (DW=8)
-      const int kb_begin = (DW == 8) ? (d >> 7) * 2 : 0;
-      const int rsw = row & 7;
-      for (int it = 0; it < nks; ++it) {
-        const int sp = it % SP;
-        const int sa = it % S;
-        mbar_wait(pk_full(sp), (it / SP) & 1, kErrWaitPackedFull);
-        mbar_wait(ab_empty(sa), ((it / S) & 1) ^ 1, kErrWaitAbEmpty);
-        const uint8_t* P = smem + C::kOffP + sp * C::kPBytes;
-        const uint32_t shb = smem[C::kOffSh + sp * C::kShBytes + row];
-        uint8_t* A = smem + C::kOffA + sa * C::kABytes + (row >> 3) * 1024 + rsw * 128;
 #pragma unroll
-        for (int kbi = 0; kbi < kKbPerThread; ++kbi) {
-          const int kb = kb_begin + kbi;
-          const uint4 w = *reinterpret_cast<const uint4*>(P + (kb * 128 + row) * 16);
-          uint32_t t0, t1;
-          decode_tables((shb >> (2 * kb)) & 3u, t0, t1);
-          uint4 lo, hi;
-          decode8(w.x, t0, t1, lo.x, hi.x);
-          decode8(w.y, t0, t1, lo.y, hi.y);
-          decode8(w.z, t0, t1, lo.z, hi.z);
-          decode8(w.w, t0, t1, lo.w, hi.w);
-          *reinterpret_cast<uint4*>(A + (((2 * kb) ^ rsw) << 4)) = lo;
-          *reinterpret_cast<uint4*>(A + (((2 * kb + 1) ^ rsw) << 4)) = hi;
+      for (int o = 16; o > 0; o >>= 1)
+        my_last = max(my_last, __shfl_xor_sync(0xffffffffu, my_last, o));
+      if (lane == 0) meta_last(ms)[warp - 2] = my_last;
+      named_bar_sync(2, 64);
+      const int n_mma = n_mma_of(ms);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(meta_full(ms));
+      if (warp == 2) {
+        // Only rows up to the last valid one are fetched (4 at a time); the
+        // MMA columns beyond hold stale data that is never stored.
+        const int last = max(meta_last(ms)[0], meta_last(ms)[1]);
+        const int n_rows = ((max(last, 0) + 4) / 4) * 4;
+        const int n_g4 = n_rows / 4;
+        for (int s = 0; s < nks; ++s, ++g) {
+          const int sb = g % S;
+          const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
+          if (lane == 0) {
+            mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+            mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * n_rows * 128));
+          }
+          __syncwarp();
+          const int x0 = (ks0 + s) * 256;
+          const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
+          // one gather4 per lane: (half, 4-row group)
+          for (int q = lane; q < nhalf * n_g4; q += 32) {
+            const int hh = q / n_g4;
+            const int r = (q - hh * n_g4) * 4;
+            // padding rows read the out-of-range row -1: zeros
+            tma_gather4(b_base + hh * C::kBHalf + (r >> 3) * 1024 + (r & 7) * 128, &p.map_act,
+                        x0 + hh * 128, src_s[r], src_s[r + 1], src_s[r + 2], src_s[r + 3],
+                        ab_full(sb), pol);
+          }
+          if (lane == 0 && g < 1024) DSV4_TRACE_EV(4, g);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(pk_empty(sp));
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(ab_full(sa));
+      } else {
+        g += nks;
       }
-
-      // ------------------------------ epilogue ------------------------------
-      mbar_wait(acc_full, 0, kErrWaitAccFull);
+      ++t;
+    }
+  } else if (warp < 8) {
+    // -------------------------------- epilogue --------------------------------
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    const int row_local = quarter * 32 + lane;
+    const int e = tid - 128;       // 0..127
+    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg);
+    const float lim = p.has_clamp ? __bfloat162float(f2bf(p.clamp_limit)) : 0.f;
+    uint32_t t = 0;
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+      const Item it = get_item(p, i, n_blocks);
+      if (!it.valid) continue;
+      int ks0, nks;
+      k_range(it, ks0, nks);
+      const int ms = t & 1;
+      const int as = t % AS;
+      mbar_wait(meta_full(ms), (t >> 1) & 1, kErrWaitMeta);
+      mbar_wait(acc_full(as), (t / AS) & 1, kErrWaitAccFull);
       tc_fence_after();
-      const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
-      const int grp = (warp - 4) >> 2;       // epilogue group (column interleave)
-      constexpr int kGroups = DW / 4;
-      const int row_local = quarter * 32 + lane;
-      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-      const float* cs_e = p.cs + static_cast<int64_t>(expert) * p.n;
+      const int* orow_s = meta_orow(ms);
+      const float* asc_s = meta_asc(ms);
+      const int n_mma = n_mma_of(ms);
+      const bool two = nks >= 2;  // issuer 1 wrote its accumulator
+      const uint32_t t0 = tmem + (as * kIssuers) * C::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+      const uint32_t t1 = t0 + C::kAccCols;
+      const float* cs_e = p.cs + static_cast<int64_t>(it.expert) * p.n;
+      auto load16 = [&](int c0, int32_t (&v)[16]) {
+        tmem_ld_x16(t0 + c0, v);
+        if (two) {
+          int32_t w[16];
+          tmem_ld_x16(t1 + c0, w);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 16; ++q) v[q] += w[q];
+        } else {
+          tmem_ld_wait();
+        }
+      };
 
       if (EPI == kEpiSwiglu) {
         const bool is_up = row_local >= 64;
         const int i_local = row_local & 63;
-        const int j0 = tile_y * 64;
+        const int j0 = it.y * 64;
         const float csn = __ldg(cs_e + (is_up ? p.inter : 0) + j0 + i_local);
-        // staging: 16 columns x 128 rows bf16, one buffer per epilogue group,
-        // in the (now idle) A ring.
-        __nv_bfloat16* stg =
-            reinterpret_cast<__nv_bfloat16*>(smem + C::kOffA) + grp * (16 * 128);
-        const int e = tid - 128 - grp * 128;  // 0..127 inside the group
-        const float lim = p.has_clamp ? __bfloat162float(f2bf(p.clamp_limit)) : 0.f;
-        for (int c0 = grp * 16; c0 < n_mma; c0 += 16 * kGroups) {
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
           int32_t v[16];
-          tmem_ld_x16(t_row + c0, v);
-          tmem_ld_wait();
+          load16(c0, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float x = __fmul_rn(__fmul_rn(__int2float_rn(v[j]), s_asc[c0 + j]), csn);
-            stg[j * 128 + row_local] = f2bf(x);
+          for (int q = 0; q < 16; ++q) {
+            const float x = __fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn);
+            stg[q * 128 + row_local] = f2bf(x);
           }
-          named_bar_sync(1 + grp, 128);
+          named_bar_sync(1, 128);
           const int col = c0 + (e >> 3);
           const int i0 = (e & 7) * 8;
-          const int orow = s_orow[col];
+          const int orow = orow_s[col];
           if (orow >= 0) {
             __align__(16) __nv_bfloat16 h[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-              float g = __bfloat162float(stg[(e >> 3) * 128 + i0 + u]);
+              float gv = __bfloat162float(stg[(e >> 3) * 128 + i0 + u]);
               float up = __bfloat162float(stg[(e >> 3) * 128 + 64 + i0 + u]);
               if (p.has_clamp) {
-                g = fminf(g, lim);
+                gv = fminf(gv, lim);
                 up = fminf(fmaxf(up, -lim), lim);
               }
-              const float sg = __bfloat162float(f2bf(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+              const float sg = __bfloat162float(f2bf(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)))));
               h[u] = f2bf(__fmul_rn(sg, up));
             }
             *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo + j0 + i0) =
                 *reinterpret_cast<const uint4*>(h);
           }
-          named_bar_sync(1 + grp, 128);
+          named_bar_sync(1, 128);
         }
       } else {
-        const int n_g = tile_y * 128 + row_local;
+        const int n_g = it.y * 128 + row_local;
         const float csn = (EPI == kEpiBf16) ? __ldg(cs_e + n_g) : 0.f;
-        for (int c0 = grp * 16; c0 < n_mma; c0 += 16 * kGroups) {
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
           int32_t v[16];
-          tmem_ld_x16(t_row + c0, v);
-          tmem_ld_wait();
+          load16(c0, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int orow = s_orow[c0 + j];
+          for (int q = 0; q < 16; ++q) {
+            const int orow = orow_s[c0 + q];
             if (orow < 0) continue;
             if (EPI == kEpiBf16) {
-              const float x = __fmul_rn(__fmul_rn(__int2float_rn(v[j]), s_asc[c0 + j]), csn);
+              const float x = __fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn);
               p.out[static_cast<int64_t>(orow) * p.ldo + n_g] = f2bf(x);
             } else {
-              p.out_i32[static_cast<int64_t>(blockIdx.z) * p.split_stride +
-                        static_cast<int64_t>(orow) * p.ldo + n_g] = v[j];
+              p.out_i32[static_cast<int64_t>(it.z) * p.split_stride +
+                        static_cast<int64_t>(orow) * p.ldo + n_g] = v[q];
             }
           }
         }
       }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(acc_empty(as));
+        mbar_arrive(meta_empty(ms));
+      }
+      ++t;
+    }
+  } else {
+    // ------------------------- FP4 -> INT8 decode -> TMEM -------------------------
+    // Two groups of 4 warps take alternate stages; in a group warp w covers TMEM
+    // lane quarter w % 4 (rows 32*(w%4) ..) and all 8 32-K blocks of the stage
+    // (64 TMEM columns: block kb -> columns 8kb .. 8kb+7).
+    const int quarter = warp & 3;
+    const int grp = (warp - 8) >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
+    uint32_t g = 0;
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+      const Item it = get_item(p, i, n_blocks);
+      if (!it.valid) continue;
+      int ks0, nks;
+      k_range(it, ks0, nks);
+      for (int s = 0; s < nks; ++s, ++g) {
+        if (static_cast<int>(g % kDecodeGroups) != grp) continue;
+        const int sp = g % SP;
+        const int sa = g % S;
+        const int nkb = stage_kb(ks0 + s);
+        mbar_wait(pk_full(sp), (g / SP) & 1, kErrWaitPackedFull);
+        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(1, g);
+        const uint8_t* P = smem + C::kOffP + sp * C::kPBytes;
+        const uint8_t* SH = smem + C::kOffSh + sp * C::kShBytes;
+        uint32_t shw[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          shw[hh] = EPI == kEpiSwiglu ? SH[(row >> 6) * 128 + hh * 64 + (row & 63)]
+                                      : SH[hh * 128 + row];
+        mbar_wait(ab_empty(sa), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, g);
+        tc_fence_after();
+        const uint32_t tcol = tmem + t_lane + C::kAColBase + sa * 64;
+        // all 8 packed units first (a 128-K tail stage decodes stale bytes
+        // into columns the MMA never reads)
+        uint4 wv[8];
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+          const int poff = EPI == kEpiSwiglu ? ((row >> 6) * 8192 + kb * 1024 + (row & 63) * 16)
+                                             : (kb * 2048 + row * 16);
+          wv[kb] = *reinterpret_cast<const uint4*>(P + poff);
+        }
+        (void)nkb;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // blocks 2q, 2q+1 -> columns 16q .. 16q+15
+          uint32_t v[16];
+#pragma unroll
+          for (int kbi = 0; kbi < 2; ++kbi) {
+            const int kb = 2 * q + kbi;
+            const uint4 w = wv[kb];
+            uint32_t a0, a1;
+            decode_tables((shw[kb >> 2] >> (2 * (kb & 3))) & 3u, a0, a1);
+            // columns 8*kbi + 0..3: k 0..15 of the block, 8*kbi + 4..7: k 16..31
+            decode8(w.x, a0, a1, v[8 * kbi + 0], v[8 * kbi + 4]);
+            decode8(w.y, a0, a1, v[8 * kbi + 1], v[8 * kbi + 5]);
+            decode8(w.z, a0, a1, v[8 * kbi + 2], v[8 * kbi + 6]);
+            decode8(w.w, a0, a1, v[8 * kbi + 3], v[8 * kbi + 7]);
+          }
+#ifdef DSV4_TRACE_NOST
+          if (v[0] == 0x12345678u && v[5] == 0x9abcdef0u) tmem_st_x16(tcol + 16 * q, v);
+#else
+          tmem_st_x16(tcol + 16 * q, v);
+#endif
+        }
+        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(7, g);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pk_empty(sp));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ab_full(sa));
+        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(5, g);
+      }
     }
   }
 
+  tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
