@@ -235,6 +235,8 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   DSV4_REQUIRE(grid_m <= 0x7FFFFFFF, "too many M tiles");
 
   TcGemmParams p{};
+  p.dec_m1 = 0xFFFFFFFFu;
+  p.dec_hi16 = 65536u;
   p.a = a_q;
   p.a_scale = a_scale;
   p.lda = k;
@@ -281,6 +283,8 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
                  int64_t ld, int64_t split_stride, int epi, void* stream) {
   if (int r = check_weights(1, n, k, shift_stride)) return r;
   TcGemmParams p{};
+  p.dec_m1 = 0xFFFFFFFFu;
+  p.dec_hi16 = 65536u;
   p.a = a_q;
   p.a_scale = a_scale;
   p.lda = k;

@@ -83,6 +83,9 @@ struct TcGemmParams {
   int64_t split_stride;
   float clamp_limit;
   int has_clamp;
+  // run-time constants of the decode (0xFFFFFFFF, 65536): see decode8_fma
+  uint32_t dec_m1;
+  uint32_t dec_hi16;
 };
 
 constexpr int kDecodeGroups = 3;                    // groups of 4 warps, alternate stages
@@ -207,7 +210,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       mbar_init(pk_empty(s), 4);
     }
     for (int s = 0; s < S; ++s) {
-      mbar_init(ab_full(s), 4 + 1);
+      mbar_init(ab_full(s), 4 + 1);  // one decode group (4 warps) + one gather lane
       mbar_init(ab_empty(s), 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -374,35 +377,35 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const int n_mma = n_mma_of(ms);
       __syncwarp();
       if (lane == 0) mbar_arrive(meta_full(ms));
-      if (warp == 2) {
-        // Only rows up to the last valid one are fetched (4 at a time); the
-        // MMA columns beyond hold stale data that is never stored.
+      {
+        // Warps 2 and 3 take alternate stages.  Only rows up to the last valid
+        // one are fetched (4 at a time, lane l -> rows 4l .. 4l+3 of both
+        // 128-K halves); the MMA columns beyond hold stale data never stored.
         const int last = max(meta_last(ms)[0], meta_last(ms)[1]);
         const int n_rows = ((max(last, 0) + 4) / 4) * 4;
-        const int n_g4 = n_rows / 4;
         for (int s = 0; s < nks; ++s, ++g) {
+          if (static_cast<int>(g & 1) != warp - 2) continue;
           const int sb = g % S;
           const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
           if (lane == 0) {
             mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+            DSV4_TRACE_EV(7, g);
             mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * n_rows * 128));
           }
           __syncwarp();
           const int x0 = (ks0 + s) * 256;
           const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
-          // one gather4 per lane: (half, 4-row group)
-          for (int q = lane; q < nhalf * n_g4; q += 32) {
-            const int hh = q / n_g4;
-            const int r = (q - hh * n_g4) * 4;
+          for (int r = lane * 4; r < n_rows; r += 128) {
+            const uint32_t dst = b_base + (r >> 3) * 1024 + (r & 7) * 128;
             // padding rows read the out-of-range row -1: zeros
-            tma_gather4(b_base + hh * C::kBHalf + (r >> 3) * 1024 + (r & 7) * 128, &p.map_act,
-                        x0 + hh * 128, src_s[r], src_s[r + 1], src_s[r + 2], src_s[r + 3],
+            tma_gather4(dst, &p.map_act, x0, src_s[r], src_s[r + 1], src_s[r + 2], src_s[r + 3],
                         ab_full(sb), pol);
+            if (nhalf == 2)
+              tma_gather4(dst + C::kBHalf, &p.map_act, x0 + 128, src_s[r], src_s[r + 1],
+                          src_s[r + 2], src_s[r + 3], ab_full(sb), pol);
           }
-          if (lane == 0 && g < 1024) DSV4_TRACE_EV(4, g);
+          if (lane == 0) DSV4_TRACE_EV(4, g);
         }
-      } else {
-        g += nks;
       }
       ++t;
     }
@@ -516,6 +519,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     const int grp = (warp - 8) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16;
     uint32_t g = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
       const Item it = get_item(p, i, n_blocks);
@@ -560,10 +564,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             uint32_t a0, a1;
             decode_tables((shw[kb >> 2] >> (2 * (kb & 3))) & 3u, a0, a1);
             // columns 8*kbi + 0..3: k 0..15 of the block, 8*kbi + 4..7: k 16..31
-            decode8(w.x, a0, a1, v[8 * kbi + 0], v[8 * kbi + 4]);
-            decode8(w.y, a0, a1, v[8 * kbi + 1], v[8 * kbi + 5]);
-            decode8(w.z, a0, a1, v[8 * kbi + 2], v[8 * kbi + 6]);
-            decode8(w.w, a0, a1, v[8 * kbi + 3], v[8 * kbi + 7]);
+            decode8_fma(w.x, a0, a1, m1, hi16, v[8 * kbi + 0], v[8 * kbi + 4]);
+            decode8_fma(w.y, a0, a1, m1, hi16, v[8 * kbi + 1], v[8 * kbi + 5]);
+            decode8_fma(w.z, a0, a1, m1, hi16, v[8 * kbi + 2], v[8 * kbi + 6]);
+            decode8_fma(w.w, a0, a1, m1, hi16, v[8 * kbi + 3], v[8 * kbi + 7]);
           }
 #ifdef DSV4_TRACE_NOST
           if (v[0] == 0x12345678u && v[5] == 0x9abcdef0u) tmem_st_x16(tcol + 16 * q, v);
@@ -571,7 +575,6 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           tmem_st_x16(tcol + 16 * q, v);
 #endif
         }
-        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(7, g);
         __syncwarp();
         if (lane == 0) mbar_arrive(pk_empty(sp));
         tmem_st_wait();
