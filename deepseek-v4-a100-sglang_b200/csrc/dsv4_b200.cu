@@ -109,7 +109,7 @@ int launch_gemm(int tn, int64_t max_items, const TcGemmParams& p, cudaStream_t s
   switch (tn) {
 #define DSV4_CASE(T)                                                                    \
   case T:                                                                               \
-    mxfp4_int8_tc_gemm_kernel<T, EPI><<<grid, kGemmThreads, GemmKernel<T, EPI>::kSmem, st>>>(p); \
+    mxfp4_int8_tc_gemm_kernel<T, EPI><<<grid, TcGemmCfg<T>::kThreads, GemmKernel<T, EPI>::kSmem, st>>>(p); \
     break;
     DSV4_CASE(16)
     DSV4_CASE(32)

@@ -22,18 +22,18 @@
 // stages of an item into two accumulators (int32 sums are exact; the
 // epilogue adds them), which halves the per-stage issue time per SM.
 //
-// Warp roles (21 warps):
+// Warp roles (per token tile, see TcGemmCfg):
 //   warp 0       TMA producer: packed FP4 codes (3-D tensor map) + 2-bit
-//                shifts (2-D tensor map), 128 K per stage, deep packed ring
-//   warp 1       TMEM allocator; MMA issuer for even stages of each item
-//   warps 2..3   per-item token metadata; warp 2 lane 0 gathers the token
-//                rows with TMA tile::gather4 into the SW128 K-major B ring
+//                shifts (2-D tensor map), 256 K per stage, deep packed ring
+//   warp 1       TMEM allocator; MMA issuer 0
+//   warps 2..3   per-item token metadata; warp 2 + (g % 2) gathers the token
+//                rows of stage g with TMA tile::gather4 into the SW128 B ring
 //   warps 4..7   epilogue: TMEM -> registers -> scales -> bf16 / int32 /
-//                SwiGLU -> global (overlaps the next item's main loop)
-//   warps 8..19  FP4 -> INT8 decode from the packed ring straight into TMEM
-//                (tcgen05.st), three groups of 4 warps taking stages in turn:
-//                one 64-column A slot per 128x256 stage
-//   warp 20      MMA issuer for odd stages of each item
+//                SwiGLU -> global
+//   warps 8..    FP4 -> INT8 decode from the packed ring straight into TMEM
+//                (tcgen05.st), kDecodeGroups groups of 4 warps, group g % G
+//                takes stage g: one 64-column A slot per 128x256 stage
+//   last warps   MMA issuers 1.. (issuer g % kIssuers takes stage g)
 #pragma once
 
 #include "common.cuh"
@@ -88,13 +88,14 @@ struct TcGemmParams {
   uint32_t dec_hi16;
 };
 
-constexpr int kDecodeGroups = 3;                    // groups of 4 warps, alternate stages
-constexpr int kDecodeWarps = 4 * kDecodeGroups;
-constexpr int kIssuer1Warp = 8 + kDecodeWarps;       // second MMA issuer
-constexpr int kGemmWarps = kIssuer1Warp + 1;
-constexpr int kGemmThreads = kGemmWarps * 32;
-constexpr int kIssuers = 2;
-
+// Ring discipline: an mbarrier parity wait is only safe if the waiter takes
+// part in every use of that slot (otherwise it can run two phases ahead and
+// see a stale phase as complete).  Every role therefore takes stage g by
+// g mod (its count), and each ring depth is a multiple of those counts, so
+// each slot always has the same waiter:
+//   decode group  g % kDecodeGroups   -> kDecodeGroups | kStages, kStagesP
+//   MMA issuer    g % kIssuers        -> kIssuers | kStages
+//   gather warp   g % 2               -> 2 | kStages
 template <int TN>
 struct TcGemmCfg {
   static constexpr int kBHalf = TN * 128;        // one 128-K SW128 sub-tile of B
@@ -103,19 +104,21 @@ struct TcGemmCfg {
   // shift slot per stage: [2 x 128 B] (plain) or gate [2 x 64 B] at +0 and up
   // [2 x 64 B] at +128 (SwiGLU); tiled TMA destinations must be 128-byte aligned
   static constexpr int kShBytes = 256;
-  // TMEM (512 columns): [issuer accumulators x slots], then 64-column A slots
   static constexpr int kAccCols = TN < 32 ? 32 : TN;
-  static constexpr int kAccSlots = TN <= 64 ? 2 : 1;
+  static constexpr int kIssuers = TN <= 32 ? 3 : 2;       // MMA issuer threads, one accumulator each
+  static constexpr int kDecodeGroups = TN <= 64 ? 3 : 4;  // groups of 4 decode warps
+  static constexpr int kAccSlots = 1;                     // accumulator sets (per issuer)
+  static constexpr int kStages = TN <= 64 ? 6 : 4;        // A (TMEM, 64 cols) + B (smem) ring
+  // TMEM (512 columns): [issuer accumulators], then 64-column A slots
   static constexpr int kAColBase = kIssuers * kAccSlots * kAccCols;
-  static constexpr int kStagesRaw = (512 - kAColBase) / 64;
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;  // A (TMEM) + B (smem) ring
   static constexpr int kTmemCols = 512;
   static constexpr int kStgBytes = 16 * 128 * 2;   // SwiGLU staging (16 cols x 128 rows bf16)
   static constexpr int kMetaBytes = TN * 12 + 16;  // src, orow, ascale, per-warp last
   static constexpr int kFixed = kStages * kBBytes + kStgBytes + 2 * kMetaBytes + 1024;
   static constexpr int kBudget = 227 * 1024 - 1024;  // minus alignment slack
   static constexpr int kStagesPRaw = (kBudget - kFixed) / (kPBytes + kShBytes);
-  static constexpr int kStagesP = kStagesPRaw > 16 ? 16 : kStagesPRaw;
+  static constexpr int kStagesPCap = kStagesPRaw > 16 ? 16 : kStagesPRaw;
+  static constexpr int kStagesP = kStagesPCap / kDecodeGroups * kDecodeGroups;
   static constexpr int kOffB = 0;
   static constexpr int kOffP = kOffB + kStages * kBBytes;
   static constexpr int kOffSh = kOffP + kStagesP * kPBytes;
@@ -127,8 +130,16 @@ struct TcGemmCfg {
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
+  // warps: 0 TMA, 1 issuer 0 + TMEM, 2-3 gather, 4-7 epilogue, decode groups, issuers 1..
+  static constexpr int kDecodeWarps = 4 * kDecodeGroups;
+  static constexpr int kIssuer1Warp = 8 + kDecodeWarps;
+  static constexpr int kWarps = kIssuer1Warp + kIssuers - 1;
+  static constexpr int kThreads = kWarps * 32;
   static_assert(TN % 16 == 0 && TN >= 16 && TN <= 128, "token tile");
-  static_assert(kStagesP >= 3 && kStages >= 4, "rings too shallow");
+  static_assert(kStages % kDecodeGroups == 0 && kStages % kIssuers == 0 && kStages % 2 == 0,
+                "ring discipline");
+  static_assert(kStagesP % kDecodeGroups == 0 && kStagesP >= 3, "packed ring");
+  static_assert(kAColBase + kStages * 64 <= kTmemCols, "TMEM budget");
   static_assert(kSmemLaunch <= 227 * 1024, "shared memory budget");
   static_assert(kBHalf % 1024 == 0 && kOffMeta % 16 == 0 && kOffBar % 8 == 0, "alignment");
 };
@@ -161,7 +172,7 @@ __device__ __forceinline__ Item get_item(const TcGemmParams& p, int i, int n_blo
 }
 
 template <int TN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(TcGemmCfg<TN>::kThreads, 1)
 mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   using C = TcGemmCfg<TN>;
   constexpr int S = C::kStages;
@@ -214,7 +225,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       mbar_init(ab_empty(s), 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(acc_full(s), kIssuers);
+      mbar_init(acc_full(s), C::kIssuers);
       mbar_init(acc_empty(s), 4);
       mbar_init(meta_full(s), 2);
       mbar_init(meta_empty(s), 4);
@@ -286,10 +297,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         }
       }
     }
-  } else if (warp == 1 || warp == kIssuer1Warp) {
+  } else if (warp == 1 || warp >= C::kIssuer1Warp) {
     // ------------------------------- MMA issuers -------------------------------
-    if (lane == 0) {
-      const int j = warp == 1 ? 0 : 1;  // this issuer takes stages s = j, j+2, ...
+    const int j = warp == 1 ? 0 : warp - C::kIssuer1Warp + 1;  // takes stages g = j (mod kIssuers)
+    if (lane == 0 && j < C::kIssuers) {
       uint32_t g = 0, t = 0;
       const uint64_t bdesc0 = smem_desc_sw128(smem_u32(smem + C::kOffB));
       for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
@@ -303,8 +314,9 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         const uint32_t idesc = idesc_i8(128, n_mma_of(ms));
         mbar_wait(acc_empty(as), ((t / AS) & 1) ^ 1, kErrWaitAccEmpty);
         tc_fence_after();
-        const uint32_t d_tmem = tmem + (as * kIssuers + j) * C::kAccCols;
-        for (int s = j; s < nks; s += 2) {
+        const uint32_t d_tmem = tmem + (as * C::kIssuers + j) * C::kAccCols;
+        const int s_first = static_cast<int>((j - static_cast<int>(g % C::kIssuers) + C::kIssuers) % C::kIssuers);
+        for (int s = s_first; s < nks; s += C::kIssuers) {
           const uint32_t gs = g + s;
           const int sa = gs % S;
           mbar_wait(ab_full(sa), (gs / S) & 1, kErrWaitAbFull);
@@ -318,7 +330,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             if (kk < nkb)
               mma_i8_ts(d_tmem, a_tmem + kk * 8,
                         bdesc + static_cast<uint64_t>(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4),
-                        idesc, (s > j || kk > 0) ? 1u : 0u);
+                        idesc, (s > s_first || kk > 0) ? 1u : 0u);
           }
           mma_commit(ab_empty(sa));
           DSV4_TRACE_EV(6, gs);
@@ -416,7 +428,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     const int e = tid - 128;       // 0..127
     __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg);
     const float lim = p.has_clamp ? __bfloat162float(f2bf(p.clamp_limit)) : 0.f;
-    uint32_t t = 0;
+    uint32_t t = 0, g = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
       const Item it = get_item(p, i, n_blocks);
       if (!it.valid) continue;
@@ -430,20 +442,21 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const int* orow_s = meta_orow(ms);
       const float* asc_s = meta_asc(ms);
       const int n_mma = n_mma_of(ms);
-      const bool two = nks >= 2;  // issuer 1 wrote its accumulator
-      const uint32_t t0 = tmem + (as * kIssuers) * C::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-      const uint32_t t1 = t0 + C::kAccCols;
+      // accumulators written: issuers (g + s) % kIssuers for s < nks
+      uint32_t accmask = 0;
+      for (int q = 0; q < min(nks, C::kIssuers); ++q) accmask |= 1u << ((g + q) % C::kIssuers);
+      const uint32_t t0 = tmem + (as * C::kIssuers) * C::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
       const float* cs_e = p.cs + static_cast<int64_t>(it.expert) * p.n;
       auto load16 = [&](int c0, int32_t (&v)[16]) {
-        tmem_ld_x16(t0 + c0, v);
-        if (two) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) v[q] = 0;
+        for (int a = 0; a < C::kIssuers; ++a) {
+          if (!(accmask & (1u << a))) continue;
           int32_t w[16];
-          tmem_ld_x16(t1 + c0, w);
+          tmem_ld_x16(t0 + a * C::kAccCols + c0, w);
           tmem_ld_wait();
 #pragma unroll
           for (int q = 0; q < 16; ++q) v[q] += w[q];
-        } else {
-          tmem_ld_wait();
         }
       };
 
@@ -508,9 +521,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         mbar_arrive(acc_empty(as));
         mbar_arrive(meta_empty(ms));
       }
+      g += nks;
       ++t;
     }
-  } else {
+  } else if (warp < C::kIssuer1Warp) {
     // ------------------------- FP4 -> INT8 decode -> TMEM -------------------------
     // Two groups of 4 warps take alternate stages; in a group warp w covers TMEM
     // lane quarter w % 4 (rows 32*(w%4) ..) and all 8 32-K blocks of the stage
@@ -527,7 +541,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       int ks0, nks;
       k_range(it, ks0, nks);
       for (int s = 0; s < nks; ++s, ++g) {
-        if (static_cast<int>(g % kDecodeGroups) != grp) continue;
+        if (static_cast<int>(g % C::kDecodeGroups) != grp) continue;
         const int sp = g % SP;
         const int sa = g % S;
         const int nkb = stage_kb(ks0 + s);

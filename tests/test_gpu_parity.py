@@ -93,9 +93,10 @@ def test_dense_i32_bit_exact(m, n, k):
     np.testing.assert_array_equal(acc.cpu().numpy().astype(np.int64), ref)
 
 
-@pytest.mark.parametrize("m", [1, 16, 100, 128, 300])
-def test_dense_bf16_bit_exact(m):
-    n, k = 256, 1024
+@pytest.mark.parametrize("m,n,k", [(1, 256, 1024), (16, 256, 1024), (100, 256, 1024),
+                                   (128, 256, 1024), (300, 256, 1024), (7, 1024, 7168),
+                                   (520, 384, 2304)])
+def test_dense_bf16_bit_exact(m, n, k):
     _, (b, sh, cs), (db, dsh, dcs) = _weights(1, n, k, 77 + m)
     x = G.randn_bf16((m, k), 5 + m)
     q, s = O.quantize_per_token_int8(x.float().numpy())
@@ -125,7 +126,10 @@ def _moe_case(e, t, h, i, topk, seed, bm):
 
 
 MOE_CASES = [(4, 13, 128, 128, 2, 16), (16, 64, 256, 128, 8, 16), (8, 40, 256, 256, 4, 32),
-             (8, 300, 128, 128, 2, 64), (8, 600, 128, 128, 2, 128)]
+             (8, 300, 128, 128, 2, 64), (8, 600, 128, 128, 2, 128),
+             # long pipelines: many 256-K stages per item and many items per CTA
+             (16, 64, 2048, 256, 8, 16), (8, 96, 1536, 384, 4, 32), (8, 256, 1152, 256, 4, 64),
+             (4, 512, 1024, 256, 2, 128)]
 
 
 @pytest.mark.parametrize("case", MOE_CASES)
