@@ -383,8 +383,25 @@ int dsv4_b200_quantize_per_token_int8(const void* a, int dtype, int64_t m, int64
                (long long)k, (long long)lda);
   if (m == 0) return DSV4_OK;
   DSV4_REQUIRE(a && a_q && a_scale, "null pointer argument");
-  const dim3 grid(static_cast<unsigned>((m + 7) / 8));
   cudaStream_t st = as_stream(stream);
+  const bool reg_ok = (dtype == DSV4_F16 || dtype == DSV4_BF16) && k % 8 == 0 && lda % 8 == 0 &&
+                      (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(a_q) & 7) == 0 && k <= 8192;
+  if (reg_ok) {
+    // register-resident rows: 128 threads per row for long rows, a warp otherwise
+    const bool wide = k > 2048;
+    const int rows_per_cta = wide ? 2 : 8;
+    const dim3 g(static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta));
+    if (dtype == DSV4_BF16) {
+      if (wide) quant_rows_reg_kernel<__nv_bfloat16, 128, 8><<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale);
+      else quant_rows_reg_kernel<__nv_bfloat16, 32, 8><<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale);
+    } else {
+      if (wide) quant_rows_reg_kernel<__half, 128, 8><<<g, 256, 0, st>>>(static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale);
+      else quant_rows_reg_kernel<__half, 32, 8><<<g, 256, 0, st>>>(static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale);
+    }
+    return check_launch("quant_rows_reg_kernel");
+  }
+  const dim3 grid(static_cast<unsigned>((m + 7) / 8));
   switch (dtype) {
     case DSV4_F32:
       quant_rows_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(a), m, k, lda,

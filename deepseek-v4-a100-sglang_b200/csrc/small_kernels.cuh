@@ -82,6 +82,68 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ a
   if (lane == 0) scale[row] = s;
 }
 
+// Register-resident variant for bf16/fp16 rows with K % 8 == 0: each row is
+// read once (uint4 per 8 elements) by RT threads (RT = 32 or 128), reduced,
+// then quantised from registers.  Same arithmetic as quant_rows_kernel.
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict__ a, int64_t m,
+                                                             int64_t k, int64_t lda,
+                                                             float clamp_abs,
+                                                             int8_t* __restrict__ q,
+                                                             float* __restrict__ scale) {
+  constexpr int kRowsPerCta = 256 / RT;
+  __shared__ float red[256 / 32];
+  const int r_local = threadIdx.x / RT;
+  const int lt = threadIdx.x % RT;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerCta + r_local;
+  const bool active = row < m;
+  const int nv = static_cast<int>(k / 8);
+  uint4 u[VPT];
+  float amax = 0.f;
+  if (active) {
+    const uint4* xv = reinterpret_cast<const uint4*>(a + row * lda);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = lt + i * RT;
+      if (idx < nv) {
+        u[i] = __ldg(xv + idx);
+        const T* e = reinterpret_cast<const T*>(&u[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(clampf_abs(to_f32<T>(e[j]), clamp_abs)));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (RT > 32) {
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    const int w0 = (r_local * RT) >> 5;
+    amax = 0.f;
+#pragma unroll
+    for (int w = 0; w < RT / 32; ++w) amax = fmaxf(amax, red[w0 + w]);
+  }
+  if (!active) return;
+  float sc = __fdiv_rn(amax, 127.0f);
+  if (sc == 0.0f) sc = 1.0f;
+  uint2* qr = reinterpret_cast<uint2*>(q + row * k);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = lt + i * RT;
+    if (idx < nv) {
+      const T* e = reinterpret_cast<const T*>(&u[i]);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(clampf_abs(to_f32<T>(e[j]), clamp_abs), sc))) << (8 * j);
+        hi |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(clampf_abs(to_f32<T>(e[j + 4]), clamp_abs), sc))) << (8 * j);
+      }
+      qr[idx] = make_uint2(lo, hi);
+    }
+  }
+  if (lt == 0) scale[row] = sc;
+}
+
 // ---------------------------------------------------------------------------
 // a5. expert align (reference call site PYMOE:842-869, library
 // sgl_kernel.moe_align_block_size).  One CTA of 1024 threads:
