@@ -34,6 +34,7 @@ for p in (str(ROOT), str(ROOT / "deepseek-v4-a100-sglang_b200"), str(ROOT / "tes
 
 H, I, E, TOPK = 7168, 2048, 256, 8
 DECODE_M, PREFILL_M = 64, 8192
+EP_PREFILL_TOKENS = 32768  # global batch split evenly across ranks
 EXP_RANGE = (-8, -4)
 
 
@@ -108,16 +109,17 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_weights(dev, seed):
+def make_weights(dev, seed, experts=None):
     """Random MXFP4 expert weights generated on the GPU, repacked there."""
+    experts = E if experts is None else experts
     import torch
     import dsv4_b200 as D
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     out = []
     for n, k in ((2 * I, H), (H, I)):
-        w = torch.randint(0, 256, (E, n, k // 2), device=dev, dtype=torch.uint8, generator=g)
-        s = torch.randint(127 + EXP_RANGE[0], 127 + EXP_RANGE[1] + 1, (E, n, k // 32), device=dev,
+        w = torch.randint(0, 256, (experts, n, k // 2), device=dev, dtype=torch.uint8, generator=g)
+        s = torch.randint(127 + EXP_RANGE[0], 127 + EXP_RANGE[1] + 1, (experts, n, k // 32), device=dev,
                           dtype=torch.uint8, generator=g)
         out.extend(D.remap_mxfp4_weight_for_int8(w, s))
         del w, s
@@ -255,6 +257,68 @@ def run_workload(weights, m, zipf, steps, warmup, dev, rank, world, hbm, tops_i8
     return res
 
 
+def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks):
+    """Expert-parallel layer: this rank holds E/world experts and m tokens."""
+    import torch
+    import torch.distributed as dist
+    import gen_inputs as G
+    from dsv4_b200.ep import ExpertParallelMoE, GpuOps
+    e_loc = E // world
+    weights = make_weights(dev, 42 + rank, e_loc)
+    layer = ExpertParallelMoE(GpuOps(weights, H, I), num_experts=E, hidden_size=H,
+                              capacity_tokens=m if m <= 256 else None)
+    ids, tw = routing(m, 1000 + rank, zipf)
+    x = G.randn_bf16((m, H), 2000 + rank)
+    xd, idd, twd = x.to(dev), ids.to(dev), tw.to(dev)
+    for _ in range(warmup):
+        layer.forward(xd, idd, twd)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = Clocks(local_gpu_index())
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with (clk if sample_clocks else _Null()):
+        start.record()
+        for _ in range(steps):
+            layer.forward(xd, idd, twd)
+        stop.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    stats = dict(layer.last_stats)
+    # end to end: pinned host buffers in, host output back, every step
+    hx, hid, htw = x.pin_memory(), ids.pin_memory(), tw.pin_memory()
+    hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        o = layer.forward(hx.to(dev, non_blocking=True), hid.to(dev, non_blocking=True),
+                          htw.to(dev, non_blocking=True))
+        hout.copy_(o, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    b13, b2 = weight_bytes_per_expert()
+    return {"ms": ms, "e2e_ms": float(t.item()), "stats": stats, "e_loc": e_loc,
+            "weight_bytes_local": e_loc * (b13 + b2), "h2d": m * H * 2 + m * TOPK * 8,
+            "d2h": m * H * 2, "clocks": clk.summary() if sample_clocks else None}
+
+
+def local_gpu_index():
+    import torch
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    cur = torch.cuda.current_device()
+    if vis:
+        try:
+            return int(vis.split(",")[cur])
+        except (ValueError, IndexError):
+            return cur
+    return cur
+
+
 class _Null:
     def __enter__(self):
         return self
@@ -334,16 +398,29 @@ def main():
         print(json.dumps(line))
         return
 
+    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
     import torch
     import torch.distributed as dist
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl")
+        # keep stdout to the single JSON line: NCCL prints its banner at init
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     dev = torch.device("cuda", local if world > 1 else torch.cuda.current_device())
     import dsv4_b200 as D  # noqa: F401
     hbm, bf16_tf, peak_src = peaks()
     tops_i8 = 2.0 * bf16_tf
 
+    if world > 1:
+        main_ep(args, dev, rank, world, hbm)
+        return
     weights = make_weights(dev, 42)
     if args.only is not None:
         m, z = (DECODE_M, None) if args.only == "decode" else (PREFILL_M, 1.1)
@@ -366,7 +443,6 @@ def main():
                "sample": "1 token of the M=64 decode batch per step (3 steps, median): dequantise its 8 "
                          "experts to fp32 + per-route SwiGLU MLP, the reference's torch CPU MoE restated"}
     if rank != 0:
-        dist.barrier() if world > 1 else None
         return
 
     total_tokens = DECODE_M * world
@@ -425,6 +501,56 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def main_ep(args, dev, rank, world, hbm):
+    import torch.distributed as dist
+    dec = run_ep(DECODE_M, None, args.steps, args.warmup, dev, rank, world, sample_clocks=(rank == 0))
+    pre = None
+    if not args.no_prefill:
+        pre = run_ep(EP_PREFILL_TOKENS // world, 1.1, max(3, args.steps // 20), args.warmup, dev, rank,
+                     world, sample_clocks=False)
+    if rank == 0:
+        total = DECODE_M * world
+        line = {
+            "metric": "MoE layer tokens/s (decode M=64)",
+            "value": total / (dec["ms"] * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": dec["ms"],
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int8 x mxfp4 -> int32 (bf16 I/O)",
+            "data": "synthetic",
+            "config": {"workload": "decode MoE layer, expert parallel: H=7168 I=2048 E=256 top-8, "
+                                   f"M=64 tokens per GPU, {E // world} experts per GPU",
+                       "parallelism": f"ep{world}", "l2": "not flushed: weights streamed per step",
+                       "collectives": "NCCL all_to_all_single (counts, int8 rows + metadata, "
+                                      "bf16 partials)",
+                       "rank0_dispatch": dec["stats"]},
+            "roofline": {"bound": "hbm", "kernel": "whole EP layer step (rank 0)",
+                         "achieved": dec["weight_bytes_local"] / (dec["ms"] * 1e-3) / 1e9,
+                         "peak": hbm, "unit": "GB/s",
+                         "frac": dec["weight_bytes_local"] / (dec["ms"] * 1e-3) / 1e9 / hbm,
+                         "traffic": None, "note": "upper bound: all local experts counted"},
+            "e2e": {"value": total / (dec["e2e_ms"] * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"],
+                    "ms_per_step": dec["e2e_ms"]},
+            "gpu_launches": (LAUNCHES_PER_STEP + 3) * args.steps,
+            "clocks": dec["clocks"],
+        }
+        if pre is not None:
+            line["prefill"] = {"workload": f"EP prefill: {EP_PREFILL_TOKENS} tokens total, Zipf(1.1)",
+                               "value": EP_PREFILL_TOKENS / (pre["ms"] * 1e-3), "unit": "tokens/s",
+                               "ms_per_step": pre["ms"],
+                               "e2e": {"value": EP_PREFILL_TOKENS / (pre["e2e_ms"] * 1e-3),
+                                       "unit": "tokens/s"}}
+        print(json.dumps(line))
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

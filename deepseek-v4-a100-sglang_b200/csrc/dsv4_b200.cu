@@ -534,6 +534,60 @@ int dsv4_b200_mxfp4_int8_moe_reduce(const void* routed_out, const float* topk_we
   return check_launch("moe_reduce_kernel");
 }
 
+int dsv4_b200_mxfp4_int8_moe_reduce_masked(const void* routed_out, const float* topk_weights,
+                                           const int32_t* topk_ids, void* out, int64_t m_out,
+                                           int64_t n, int64_t topk, int64_t num_valid_tokens,
+                                           int apply_scaling, float routed_scaling_factor,
+                                           void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(n > 0 && n % 8 == 0, "reduce requires N divisible by 8, got %lld", (long long)n);
+  DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
+  DSV4_REQUIRE(num_valid_tokens >= 0 && m_out * topk >= num_valid_tokens,
+               "out rows do not cover routed slots");
+  if (m_out == 0) return DSV4_OK;
+  DSV4_REQUIRE(routed_out && topk_weights && topk_ids && out, "null pointer argument");
+  const int64_t threads = m_out * (n / 8);
+  moe_reduce_masked_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
+                             as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(routed_out), topk_weights, topk_ids,
+      static_cast<__nv_bfloat16*>(out), static_cast<int>(m_out), static_cast<int>(n),
+      static_cast<int>(topk), static_cast<int>(num_valid_tokens), routed_scaling_factor,
+      apply_scaling ? 1 : 0);
+  return check_launch("moe_reduce_masked_kernel");
+}
+
+int dsv4_b200_gather_rows(const void* src, int64_t row_bytes, const int64_t* idx, int64_t n_rows,
+                          void* dst, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(row_bytes > 0 && row_bytes % 16 == 0, "row_bytes must be a multiple of 16");
+  DSV4_REQUIRE(n_rows >= 0, "bad n_rows");
+  if (n_rows == 0) return DSV4_OK;
+  DSV4_REQUIRE(src && idx && dst, "null pointer argument");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0,
+               "rows must be 16-byte aligned");
+  const int64_t total = n_rows * (row_bytes / 16);
+  const int64_t blocks = (total + 255) / 256 < 65535 ? (total + 255) / 256 : 65535;
+  gather_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(src), row_bytes, idx, n_rows, static_cast<uint8_t*>(dst));
+  return check_launch("gather_rows_kernel");
+}
+
+int dsv4_b200_ep_combine(const void* partial, const int64_t* pos, int64_t world, void* out,
+                         int64_t m, int64_t n, int apply_scaling, float routed_scaling_factor,
+                         void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(n > 0 && n % 8 == 0, "combine requires N divisible by 8");
+  DSV4_REQUIRE(world >= 1 && m >= 0, "bad world/m");
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(pos && out, "null pointer argument");
+  const int64_t threads = m * (n / 8);
+  ep_combine_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(partial), pos, static_cast<int>(world),
+      static_cast<__nv_bfloat16*>(out), static_cast<int>(m), static_cast<int>(n),
+      routed_scaling_factor, apply_scaling ? 1 : 0);
+  return check_launch("ep_combine_kernel");
+}
+
 int dsv4_b200_mxfp4_int8_dense_gemm(const int8_t* a_q, const float* a_scale, int64_t m,
                                     int64_t k, const uint8_t* b_mxfp4, const uint8_t* b_shift2,
                                     int64_t shift_stride, const float* b_channel_scale, int64_t n,

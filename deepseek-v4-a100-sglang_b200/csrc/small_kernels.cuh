@@ -380,6 +380,90 @@ __global__ void moe_reduce_kernel(const __nv_bfloat16* __restrict__ routed,
   reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * n)[c] = *reinterpret_cast<uint4*>(o);
 }
 
+// Top-k combine that skips slots whose expert id is negative (expert held by
+// another rank under expert parallelism; their routed rows are never
+// written).  Otherwise identical to moe_reduce_kernel.
+__global__ void moe_reduce_masked_kernel(const __nv_bfloat16* __restrict__ routed,
+                                         const float* __restrict__ w,
+                                         const int32_t* __restrict__ ids,
+                                         __nv_bfloat16* __restrict__ out, int m_out, int n,
+                                         int topk, int num_valid, float rsf, int apply_rsf) {
+  const int chunks = n / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(m_out) * chunks) return;
+  const int t = static_cast<int>(idx / chunks);
+  const int c = static_cast<int>(idx - static_cast<int64_t>(t) * chunks);
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    const int slot = t * topk + k;
+    if (slot >= num_valid || __ldg(ids + slot) < 0) continue;
+    const float wt = __ldg(w + slot);
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(routed + static_cast<int64_t>(slot) * n) + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(__bfloat162float(e[i]), wt, acc[i]);
+  }
+  __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    __nv_bfloat16 b = __float2bfloat16_rn(acc[i]);
+    if (apply_rsf) b = __float2bfloat16_rn(__fmul_rn(__bfloat162float(b), rsf));
+    o[i] = b;
+  }
+  reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * n)[c] = *reinterpret_cast<uint4*>(o);
+}
+
+// Row gather: dst[i] = src[idx[i]] for rows of row_bytes (multiple of 16).
+__global__ void gather_rows_kernel(const uint8_t* __restrict__ src, int64_t row_bytes,
+                                   const int64_t* __restrict__ idx, int64_t n_rows,
+                                   uint8_t* __restrict__ dst) {
+  const int64_t vec = row_bytes / 16;
+  const int64_t total = n_rows * vec;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / vec;
+    const int64_t c = i - r * vec;
+    const int64_t s = __ldg(idx + r);
+    reinterpret_cast<uint4*>(dst + r * row_bytes)[c] =
+        __ldg(reinterpret_cast<const uint4*>(src + s * row_bytes) + c);
+  }
+}
+
+// Expert-parallel combine: out[t] = bf16(sum_r f32(partial[pos[t][r]])) over
+// r = 0..world-1 in rank order (pos -1 = no partial from rank r), then the
+// optional routed scaling in bf16.  One thread per (token, 8 columns).
+__global__ void ep_combine_kernel(const __nv_bfloat16* __restrict__ partial,
+                                  const int64_t* __restrict__ pos, int world,
+                                  __nv_bfloat16* __restrict__ out, int m, int n, float rsf,
+                                  int apply_rsf) {
+  const int chunks = n / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(m) * chunks) return;
+  const int t = static_cast<int>(idx / chunks);
+  const int c = static_cast<int>(idx - static_cast<int64_t>(t) * chunks);
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int r = 0; r < world; ++r) {
+    const int64_t p = __ldg(pos + static_cast<int64_t>(t) * world + r);
+    if (p < 0) continue;
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(partial + p * n) + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __bfloat162float(e[i]));
+  }
+  __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    __nv_bfloat16 b = __float2bfloat16_rn(acc[i]);
+    if (apply_rsf) b = __float2bfloat16_rn(__fmul_rn(__bfloat162float(b), rsf));
+    o[i] = b;
+  }
+  reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * n)[c] = *reinterpret_cast<uint4*>(o);
+}
+
 // Dense split-K reduce: out = bf16((f32(sum_s partial) * a[m]) * cs[n])
 // (reference DENSE_ENTRY:56-112).
 __global__ void splitk_reduce_kernel(const int32_t* __restrict__ partial, int splits,

@@ -282,24 +282,68 @@ def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWei
     block_m, block_n = _select_moe_tile_shape(m, topk, experts)
     sorted_ids, expert_ids, ntpp = moe_align_block_size(topk_ids_i32, block_m, experts)
     a13_q, a13_scale = quantize_per_token_int8(hidden_states, 0.0)
-    inter = torch.empty((m * topk, intermediate_size), device=hidden_states.device,
-                        dtype=torch.bfloat16)
+    return _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids,
+                     expert_ids, ntpp, block_m=block_m, block_n=block_n, hidden_size=hidden_size,
+                     intermediate_size=intermediate_size,
+                     routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
+                     masked=False)
+
+
+def _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids, expert_ids,
+              ntpp, *, block_m, block_n, hidden_size, intermediate_size, routed_scaling_factor,
+              clamp_limit, masked):
+    m = a13_q.shape[0]
+    topk = topk_ids_i32.shape[1]
+    dev = a13_q.device
+    inter = torch.empty((m * topk, intermediate_size), device=dev, dtype=torch.bfloat16)
     mxfp4_int8_moe_gemm_swiglu(
         a13_q, a13_scale, weights.w13_mxfp4, weights.w13_shift2, weights.w13_channel_scale,
         inter, sorted_ids, expert_ids, ntpp, hidden_size=hidden_size,
         intermediate_size=intermediate_size, topk=topk, block_m=block_m,
         num_valid_tokens=m * topk, clamp_limit=clamp_limit)
     a2_q, a2_scale = quantize_per_token_int8(inter, 0.0)
-    out = torch.empty((m, hidden_size), device=hidden_states.device, dtype=torch.bfloat16)
-    routed_out = torch.empty((m * topk, hidden_size), device=hidden_states.device,
-                             dtype=torch.bfloat16)
+    out = torch.empty((m, hidden_size), device=dev, dtype=torch.bfloat16)
+    routed_out = torch.empty((m * topk, hidden_size), device=dev, dtype=torch.bfloat16)
     mxfp4_int8_moe_gemm(
         a2_q, a2_scale, weights.w2_mxfp4, weights.w2_shift2, weights.w2_channel_scale, out,
         topk_weights_f32, sorted_ids, expert_ids, ntpp, hidden_size=hidden_size,
         intermediate_size=intermediate_size, topk=topk, block_m=block_m, block_n=block_n,
         source_rows_are_slots=True, num_valid_tokens=m * topk, routed_out=routed_out)
-    mxfp4_int8_moe_reduce(routed_out, topk_weights_f32, out, hidden_size=hidden_size,
-                          intermediate_size=intermediate_size, topk=topk, block_m=block_m,
-                          block_n=block_n, num_valid_tokens=m * topk,
-                          routed_scaling_factor=routed_scaling_factor)
+    if masked:
+        apply = routed_scaling_factor is not None and routed_scaling_factor != 1.0
+        N.call("dsv4_b200_mxfp4_int8_moe_reduce_masked", routed_out.data_ptr(),
+               topk_weights_f32.data_ptr(), topk_ids_i32.data_ptr(), out.data_ptr(), m,
+               hidden_size, topk, m * topk, 1 if apply else 0,
+               float(routed_scaling_factor) if apply else 1.0, N.stream_of(out))
+    else:
+        mxfp4_int8_moe_reduce(routed_out, topk_weights_f32, out, hidden_size=hidden_size,
+                              intermediate_size=intermediate_size, topk=topk, block_m=block_m,
+                              block_n=block_n, num_valid_tokens=m * topk,
+                              routed_scaling_factor=routed_scaling_factor)
     return out
+
+
+def mxfp4_int8_moe_forward_quantized(a_q: torch.Tensor, a_scale: torch.Tensor,
+                                     weights: Mxfp4Int8MoeWeights, topk_ids: torch.Tensor,
+                                     topk_weights: torch.Tensor, *, hidden_size: int,
+                                     intermediate_size: int,
+                                     routed_scaling_factor: float | None = None,
+                                     clamp_limit: float | None = None) -> torch.Tensor:
+    """MoE layer on rows that are already INT8-quantised (``a_q``, ``a_scale``),
+    as they arrive from the expert-parallel dispatch.  ``topk_ids`` index the
+    local experts of ``weights``; negative ids (experts held by other ranks)
+    contribute nothing.  Same arithmetic as mxfp4_int8_moe_forward."""
+    _require_cuda(a_q, "a_q")
+    ids = topk_ids.to(torch.int32).contiguous()
+    w = topk_weights.to(torch.float32).contiguous()
+    m, topk = ids.shape
+    experts = weights.w13_mxfp4.shape[0]
+    if m == 0:
+        return torch.empty((0, hidden_size), device=a_q.device, dtype=torch.bfloat16)
+    block_m, block_n = _select_moe_tile_shape(m, topk, experts)
+    sorted_ids, expert_ids, ntpp = moe_align_block_size(ids, block_m, experts)
+    return _moe_core(a_q.contiguous(), a_scale.contiguous(), weights, ids, w, sorted_ids,
+                     expert_ids, ntpp, block_m=block_m, block_n=block_n, hidden_size=hidden_size,
+                     intermediate_size=intermediate_size,
+                     routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
+                     masked=True)

@@ -134,6 +134,30 @@ DSV4_API int dsv4_b200_mxfp4_int8_moe_reduce(const void* routed_out, const float
                                     int64_t num_valid_tokens, int apply_scaling,
                                     float routed_scaling_factor, void* stream);
 
+/* a9 under expert parallelism: the top-k combine of dsv4_b200_mxfp4_int8_moe_reduce
+ * that skips slots whose topk_ids entry is negative (experts held by another
+ * rank; their routed_out rows are never written).  The reference has no
+ * expert parallelism; this extends mxfp4_int8_moe_reduce (JITMOE:196-225). */
+DSV4_API int dsv4_b200_mxfp4_int8_moe_reduce_masked(const void* routed_out,
+                                                    const float* topk_weights,
+                                                    const int32_t* topk_ids, void* out,
+                                                    int64_t m_out, int64_t n, int64_t topk,
+                                                    int64_t num_valid_tokens, int apply_scaling,
+                                                    float routed_scaling_factor, void* stream);
+
+/* Expert-parallel dispatch packing: dst[i] = src[idx[i]] for rows of
+ * row_bytes (multiple of 16, 16-byte aligned rows).  New component: the
+ * reference has no expert parallelism. */
+DSV4_API int dsv4_b200_gather_rows(const void* src, int64_t row_bytes, const int64_t* idx,
+                                   int64_t n_rows, void* dst, void* stream);
+
+/* Expert-parallel combine: out[t] = bf16(sum over r = 0..world-1, in rank
+ * order, of f32(partial[pos[t][r]])) for pos >= 0, then optional routed
+ * scaling (bf16).  partial: bf16 rows of n; pos: int64 [m][world]. */
+DSV4_API int dsv4_b200_ep_combine(const void* partial, const int64_t* pos, int64_t world,
+                                  void* out, int64_t m, int64_t n, int apply_scaling,
+                                  float routed_scaling_factor, void* stream);
+
 /* a11. Dense MXFP4 x INT8 GEMM: out[m][n] = bf16((f32(acc) * a_scale[m]) *
  * cs[n]).  `partial` (int32 [partial_splits][m][partial_ld]) is the
  * caller-provided split-K workspace used when m <= 128 (NULL disables
