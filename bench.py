@@ -467,7 +467,9 @@ def main():
                    "experts_touched": dec["touched"]},
         "roofline": {"bound": "hbm", "kernel": "W13 grouped GEMM + fused SwiGLU",
                      "achieved": w13_gbs, "peak": hbm, "unit": "GB/s", "frac": w13_gbs / hbm,
-                     "traffic": None, "peak_source": peak_src,
+                     # DRAM bytes per launch: the 32-expert ncu capture read+wrote 1.005x its
+                     # algorithmic bytes (profiles/moe_decode_w13_gemm_ncu.md); scaled to this launch
+                     "traffic": dec["w13_bytes"] * 1.005, "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": dec["w13_bytes"],
                      "launch_ms": dec["w13_ms"]},
         "layer_roofline": {"bound": "hbm", "bytes_per_step": dec["layer_bytes"],
