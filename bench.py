@@ -273,10 +273,12 @@ def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks):
     for _ in range(warmup):
         layer.forward(xd, idd, twd)
     torch.cuda.synchronize()
-    dist.barrier()
     clk = Clocks(local_gpu_index())
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with (clk if sample_clocks else _Null()):
+        # the sampler is up before the barrier, so no rank waits on another's start-up
+        dist.barrier()
+        torch.cuda.synchronize()
         start.record()
         for _ in range(steps):
             layer.forward(xd, idd, twd)

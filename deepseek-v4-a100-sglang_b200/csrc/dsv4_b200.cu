@@ -572,6 +572,25 @@ int dsv4_b200_gather_rows(const void* src, int64_t row_bytes, const int64_t* idx
   return check_launch("gather_rows_kernel");
 }
 
+int dsv4_b200_ep_plan_fixed(const int32_t* topk_ids, const float* topk_weights,
+                            const float* a_scale, int64_t m, int64_t topk, int64_t num_experts,
+                            int64_t world, int64_t capacity, int64_t* send_src,
+                            int32_t* send_meta, int64_t meta_words, int64_t* pos, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(world >= 1 && world <= 8 && num_experts % world == 0,
+               "world must be in [1, 8] and divide num_experts");
+  DSV4_REQUIRE(m >= 0 && m <= capacity && capacity <= kEpPlanThreads,
+               "need m <= capacity <= %d", kEpPlanThreads);
+  DSV4_REQUIRE(topk >= 1 && topk <= 8 && meta_words >= 1 + 2 * topk, "bad topk / meta width");
+  DSV4_REQUIRE(send_src && send_meta && pos && (m == 0 || (topk_ids && topk_weights && a_scale)),
+               "null pointer argument");
+  ep_plan_fixed_kernel<<<1, kEpPlanThreads, 0, as_stream(stream)>>>(
+      topk_ids, topk_weights, a_scale, static_cast<int>(m), static_cast<int>(topk),
+      static_cast<int>(num_experts), static_cast<int>(world), static_cast<int>(capacity),
+      send_src, send_meta, static_cast<int>(meta_words), pos);
+  return check_launch("ep_plan_fixed_kernel");
+}
+
 int dsv4_b200_ep_combine(const void* partial, const int64_t* pos, int64_t world, void* out,
                          int64_t m, int64_t n, int apply_scaling, float routed_scaling_factor,
                          void* stream) {

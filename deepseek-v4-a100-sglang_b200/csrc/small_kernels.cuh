@@ -464,6 +464,66 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* __restrict__ partial,
   reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * n)[c] = *reinterpret_cast<uint4*>(o);
 }
 
+// Expert-parallel plan for the fixed-capacity exchange (one CTA, m <= 1024
+// tokens, world <= 8).  For token t and rank r holding one of its experts,
+// the row goes to slot r*capacity + (number of earlier tokens that also go to
+// r).  Outputs, per slot: the source token (0 for padding), a metadata row
+// {scale, topk local expert ids (-1 = not on r / padding), topk weights};
+// per token: pos[t][r] = slot or -1.
+constexpr int kEpPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kEpPlanThreads, 1)
+ep_plan_fixed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                     const float* __restrict__ a_scale, int m, int topk, int num_experts,
+                     int world, int capacity, int64_t* __restrict__ send_src,
+                     int32_t* __restrict__ meta, int meta_words, int64_t* __restrict__ pos) {
+  __shared__ int warp_cnt[8][32];
+  const int t = threadIdx.x;
+  const int lane = t & 31, wid = t >> 5;
+  const int e_loc = num_experts / world;
+  // padding defaults for every slot
+  for (int sidx = t; sidx < world * capacity; sidx += kEpPlanThreads) {
+    send_src[sidx] = 0;
+    int32_t* row = meta + static_cast<int64_t>(sidx) * meta_words;
+    for (int c = 0; c < meta_words; ++c) row[c] = (c >= 1 && c <= topk) ? -1 : 0;
+  }
+  uint32_t has = 0;
+  if (t < m) {
+    for (int k = 0; k < topk; ++k) {
+      const int e = ids[t * topk + k];
+      if (e >= 0 && e < num_experts) has |= 1u << (e / e_loc);
+    }
+  }
+  int rank_in[8];
+  for (int r = 0; r < world; ++r) {
+    const unsigned b = __ballot_sync(0xffffffffu, (has >> r) & 1u);
+    rank_in[r] = __popc(b & ((1u << lane) - 1u));
+    if (lane == 0) warp_cnt[r][wid] = __popc(b);
+  }
+  __syncthreads();
+  if (t < m) {
+    for (int r = 0; r < world; ++r) {
+      int64_t slot = -1;
+      if ((has >> r) & 1u) {
+        int before = 0;
+        for (int q = 0; q < wid; ++q) before += warp_cnt[r][q];
+        const int j = before + rank_in[r];
+        slot = static_cast<int64_t>(r) * capacity + j;
+        send_src[slot] = t;
+        int32_t* row = meta + slot * meta_words;
+        row[0] = __float_as_int(a_scale[t]);
+        for (int k = 0; k < topk; ++k) {
+          const int e = ids[t * topk + k];
+          const bool mine = e >= 0 && e < num_experts && e / e_loc == r;
+          row[1 + k] = mine ? e - r * e_loc : -1;
+          row[1 + topk + k] = __float_as_int(mine ? w[t * topk + k] : 0.f);
+        }
+      }
+      pos[static_cast<int64_t>(t) * world + r] = slot;
+    }
+  }
+}
+
 // Dense split-K reduce: out = bf16((f32(sum_s partial) * a[m]) * cs[n])
 // (reference DENSE_ENTRY:56-112).
 __global__ void splitk_reduce_kernel(const int32_t* __restrict__ partial, int splits,

@@ -42,6 +42,7 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_mxfp4_int8_moe_reduce": [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P],
     "dsv4_b200_mxfp4_int8_moe_reduce_masked": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P],
     "dsv4_b200_gather_rows": [_P, _I64, _P, _I64, _P, _P],
+    "dsv4_b200_ep_plan_fixed": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P],
     "dsv4_b200_ep_combine": [_P, _P, _I64, _P, _I64, _I64, _I, _F, _P],
     "dsv4_b200_mxfp4_int8_dense_gemm": [_P, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _P,
                                         _I64, _I64, _P],

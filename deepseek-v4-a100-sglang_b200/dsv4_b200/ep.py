@@ -131,6 +131,22 @@ class GpuOps:
                                                 hidden_size=self.h, intermediate_size=self.i,
                                                 clamp_limit=self.clamp)
 
+    def plan_fixed(self, topk_ids, topk_weights, a_scale, num_experts, world, capacity):
+        """Device-side plan of the fixed-capacity exchange (no host sync):
+        (send_src int64 [world*cap], send_meta int32 [world*cap, W], pos [m, world])."""
+        m, topk = topk_ids.shape
+        dev = topk_ids.device
+        ids = topk_ids.to(torch.int32).contiguous()
+        w = topk_weights.to(torch.float32).contiguous()
+        n = world * capacity
+        send_src = torch.empty((n,), dtype=torch.int64, device=dev)
+        meta = torch.empty((n, _meta_width(topk)), dtype=torch.int32, device=dev)
+        pos = torch.empty((m, world), dtype=torch.int64, device=dev)
+        N.call("dsv4_b200_ep_plan_fixed", ids.data_ptr() if m else None, w.data_ptr() if m else None,
+               a_scale.data_ptr() if m else None, m, topk, num_experts, world, capacity,
+               send_src.data_ptr(), meta.data_ptr(), meta.shape[1], pos.data_ptr(), N.stream_of(pos))
+        return send_src, meta, pos
+
     def combine(self, partial, pos, m, rsf):
         out = torch.empty((m, self.h), dtype=torch.bfloat16, device=pos.device)
         apply = rsf is not None and rsf != 1.0
@@ -169,22 +185,29 @@ class ExpertParallelMoE:
                 topk_weights: torch.Tensor) -> torch.Tensor:
         m, topk = topk_ids.shape
         a_q, a_scale = self.ops.quantize(hidden)
-        plan = plan_dispatch(topk_ids, topk_weights, self.num_experts, self.world)
         dev = a_q.device
+        send_list = recv_list = None
         if self.capacity is not None:
             if m > self.capacity:
                 raise ValueError(f"{m} tokens exceed capacity_tokens={self.capacity}")
             cap = self.capacity
-            padded = pad_plan(plan, self.world, cap)
-            n_send = self.world * cap
-            send_rows = torch.zeros((n_send, a_q.shape[1]), dtype=a_q.dtype, device=dev)
-            send_rows[padded] = self.ops.gather_rows(a_q, plan.send_token)
-            meta = torch.zeros((n_send, _meta_width(topk)), dtype=torch.int32, device=dev)
-            meta[:, 1:1 + topk] = -1
-            meta[padded] = pack_meta(a_scale[plan.send_token], plan.send_lids, plan.send_w)
-            send_list = recv_list = None
-            n_recv = n_send
+            n_send = n_recv = self.world * cap
+            if hasattr(self.ops, "plan_fixed"):
+                # device-side plan (one kernel): no host synchronisation in the step
+                send_src, meta, pos = self.ops.plan_fixed(topk_ids, topk_weights, a_scale,
+                                                          self.num_experts, self.world, cap)
+                send_rows = self.ops.gather_rows(a_q, send_src)
+            else:
+                plan = plan_dispatch(topk_ids, topk_weights, self.num_experts, self.world)
+                padded = pad_plan(plan, self.world, cap)
+                send_rows = torch.zeros((n_send, a_q.shape[1]), dtype=a_q.dtype, device=dev)
+                send_rows[padded] = self.ops.gather_rows(a_q, plan.send_token)
+                meta = torch.zeros((n_send, _meta_width(topk)), dtype=torch.int32, device=dev)
+                meta[:, 1:1 + topk] = -1
+                meta[padded] = pack_meta(a_scale[plan.send_token], plan.send_lids, plan.send_w)
+                pos = plan.pos
         else:
+            plan = plan_dispatch(topk_ids, topk_weights, self.num_experts, self.world)
             # 1. counts (read back to size the exchange)
             recv_counts = torch.empty_like(plan.send_counts)
             self._a2a(recv_counts, plan.send_counts, None, None)
@@ -194,6 +217,7 @@ class ExpertParallelMoE:
             n_send = plan.send_token.numel()
             send_rows = self.ops.gather_rows(a_q, plan.send_token)
             meta = pack_meta(a_scale[plan.send_token], plan.send_lids, plan.send_w)
+            pos = plan.pos
         # 2. rows + metadata
         recv_rows = torch.empty((n_recv, a_q.shape[1]), dtype=a_q.dtype, device=dev)
         recv_meta = torch.empty((n_recv, meta.shape[1]), dtype=meta.dtype, device=dev)
@@ -208,4 +232,4 @@ class ExpertParallelMoE:
         self.last_stats = {"sent_rows": int(n_send), "recv_rows": n_recv,
                            "dispatch_bytes": int(send_rows.numel() + meta.numel() * 4),
                            "combine_bytes": int(back.numel() * 2)}
-        return self.ops.combine(back, plan.pos, m, self.rsf)
+        return self.ops.combine(back, pos, m, self.rsf)

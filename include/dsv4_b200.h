@@ -151,6 +151,20 @@ DSV4_API int dsv4_b200_mxfp4_int8_moe_reduce_masked(const void* routed_out,
 DSV4_API int dsv4_b200_gather_rows(const void* src, int64_t row_bytes, const int64_t* idx,
                                    int64_t n_rows, void* dst, void* stream);
 
+/* Expert-parallel plan for the fixed-capacity exchange (new component: the
+ * reference has no expert parallelism).  For each token t (m <= capacity <=
+ * 1024) and each rank r (world <= 8, experts split contiguously) that holds
+ * one of its top-k experts: slot r*capacity + (earlier tokens bound for r).
+ * Writes send_src [world*capacity] (token per slot, 0 for padding),
+ * send_meta int32 [world*capacity][meta_words] = {scale bits, topk local
+ * expert ids (-1 = elsewhere / padding), topk weight bits}, and
+ * pos int64 [m][world] (slot or -1). */
+DSV4_API int dsv4_b200_ep_plan_fixed(const int32_t* topk_ids, const float* topk_weights,
+                                     const float* a_scale, int64_t m, int64_t topk,
+                                     int64_t num_experts, int64_t world, int64_t capacity,
+                                     int64_t* send_src, int32_t* send_meta, int64_t meta_words,
+                                     int64_t* pos, void* stream);
+
 /* Expert-parallel combine: out[t] = bf16(sum over r = 0..world-1, in rank
  * order, of f32(partial[pos[t][r]])) for pos >= 0, then optional routed
  * scaling (bf16).  partial: bf16 rows of n; pos: int64 [m][world]. */

@@ -225,3 +225,26 @@ def test_device_status_clean_after_suite():
     from dsv4_b200 import _native as N
     torch.cuda.synchronize()
     assert N.device_status() == 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("m", [1, 37, 64, 256])
+def test_ep_plan_fixed_matches_torch_plan(world, m):
+    """The one-kernel fixed-capacity EP plan equals the torch plan + padding."""
+    from dsv4_b200.ep import GpuOps, plan_dispatch, pad_plan, pack_meta, _meta_width
+    e, topk, cap = 64, 8, 256
+    ids, tw = G.routing_sigmoid_bias_topk(m, e, topk, 900 + m)
+    ids[0, 0] = -1
+    a_scale = torch.rand(m) + 0.1
+    ops = GpuOps(None, 128, 128)
+    src, meta, pos = ops.plan_fixed(ids.cuda(), tw.cuda(), a_scale.cuda(), e, world, cap)
+    plan = plan_dispatch(ids, tw, e, world)
+    padded = pad_plan(plan, world, cap)
+    ref_meta = torch.zeros((world * cap, _meta_width(topk)), dtype=torch.int32)
+    ref_meta[:, 1:1 + topk] = -1
+    ref_meta[padded] = pack_meta(a_scale[plan.send_token], plan.send_lids, plan.send_w)
+    ref_src = torch.zeros(world * cap, dtype=torch.int64)
+    ref_src[padded] = plan.send_token
+    np.testing.assert_array_equal(pos.cpu().numpy(), plan.pos.numpy())
+    np.testing.assert_array_equal(src.cpu().numpy(), ref_src.numpy())
+    np.testing.assert_array_equal(meta.cpu().numpy(), ref_meta.numpy())
