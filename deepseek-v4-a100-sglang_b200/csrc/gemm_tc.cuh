@@ -155,9 +155,11 @@ struct Item {
 __device__ __forceinline__ Item get_item(const TcGemmParams& p, int i, int n_blocks) {
   Item it;
   if (p.moe) {
+    // row tile fastest: CTAs running side by side stream neighbouring 2 KB
+    // pieces of the same expert's K blocks
     it.z = 0;
-    it.b = i % n_blocks;
-    it.y = i / n_blocks;
+    it.y = i % p.row_tiles;
+    it.b = i / p.row_tiles;
     it.expert = __ldg(p.expert_ids + it.b);
     it.valid = it.expert >= 0;
   } else {
@@ -554,10 +556,6 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         for (int hh = 0; hh < 2; ++hh)
           shw[hh] = EPI == kEpiSwiglu ? SH[(row >> 6) * 128 + hh * 64 + (row & 63)]
                                       : SH[hh * 128 + row];
-        mbar_wait(ab_empty(sa), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
-        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, g);
-        tc_fence_after();
-        const uint32_t tcol = tmem + t_lane + C::kAColBase + sa * 64;
         // all 8 packed units first (a 128-K tail stage decodes stale bytes
         // into columns the MMA never reads)
         uint4 wv[8];
@@ -568,6 +566,15 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           wv[kb] = *reinterpret_cast<const uint4*>(P + poff);
         }
         (void)nkb;
+        // The packed slot is free once it is in registers: hand it back to the
+        // TMA producer now, not after the decode (the arrive has release
+        // semantics, ordering the loads above).
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pk_empty(sp));
+        mbar_wait(ab_empty(sa), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, g);
+        tc_fence_after();
+        const uint32_t tcol = tmem + t_lane + C::kAColBase + sa * 64;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {  // blocks 2q, 2q+1 -> columns 16q .. 16q+15
           uint32_t v[16];
@@ -589,8 +596,6 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           tmem_st_x16(tcol + 16 * q, v);
 #endif
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(pk_empty(sp));
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
