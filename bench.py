@@ -143,7 +143,6 @@ class Layer:
         import dsv4_b200 as D
         self.D, self.w, self.m, self.dev = D, weights, m, dev
         self.bm, self.bn = D.select_mxfp4_int8_moe_tile_shape(m, TOPK, E)
-        self.inter = torch.empty((m * TOPK, I), device=dev, dtype=torch.bfloat16)
         self.routed = torch.empty((m * TOPK, H), device=dev, dtype=torch.bfloat16)
         self.out = torch.empty((m, H), device=dev, dtype=torch.bfloat16)
         self.ev = []
@@ -152,23 +151,24 @@ class Layer:
         import torch
         import dsv4_b200.jit_ops as J
         D, w, m = self.D, self.w, self.m
+        kw = dict(hidden_size=H, intermediate_size=I, topk=TOPK, block_m=self.bm,
+                  num_valid_tokens=m * TOPK)
         s, e, n = D.moe_align_block_size(ids, self.bm, E)
         q, qs = D.quantize_per_token_int8(x)
+        a13, s13, r13 = J.moe_sort_rows(q, qs, s, n, topk=TOPK, num_valid_tokens=m * TOPK)
+        inter = torch.empty((s.numel(), I), device=self.dev, dtype=torch.bfloat16)
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
         if record:
             evs[0].record()
-        J.mxfp4_int8_moe_gemm_swiglu(q, qs, w.w13_mxfp4, w.w13_shift2, w.w13_channel_scale,
-                                     self.inter, s, e, n, hidden_size=H, intermediate_size=I,
-                                     topk=TOPK, block_m=self.bm, num_valid_tokens=m * TOPK)
+        J.mxfp4_int8_moe_gemm_swiglu_sorted(a13, s13, r13, w.w13_mxfp4, w.w13_shift2,
+                                            w.w13_channel_scale, inter, s, e, n, **kw)
         if record:
             evs[1].record()
-        q2, qs2 = D.quantize_per_token_int8(self.inter)
+        q2, qs2, r2 = J.quantize_sorted_int8(inter, s, n, num_valid_tokens=m * TOPK)
         if record:
             evs[2].record()
-        J.mxfp4_int8_moe_gemm(q2, qs2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale, self.out, tw,
-                              s, e, n, hidden_size=H, intermediate_size=I, topk=TOPK,
-                              block_m=self.bm, block_n=self.bn, source_rows_are_slots=True,
-                              num_valid_tokens=m * TOPK, routed_out=self.routed)
+        J.mxfp4_int8_moe_gemm_sorted(q2, qs2, r2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale,
+                                     self.routed, s, e, n, **kw)
         if record:
             evs[3].record()
             self.ev.append(evs)
@@ -182,7 +182,7 @@ class Layer:
         return statistics.mean(w13), statistics.mean(w2)
 
 
-LAUNCHES_PER_STEP = 6  # align, quant, W13+SwiGLU, quant, W2, combine
+LAUNCHES_PER_STEP = 7  # align, quant, sort rows, W13+SwiGLU, quant, W2, combine
 
 
 def routing(m, seed, zipf):

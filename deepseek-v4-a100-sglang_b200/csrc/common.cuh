@@ -53,7 +53,7 @@ __device__ __forceinline__ bool device_error_pending() {
 // CTA 0 records clock64 at each hand-off of the first kTraceStages stages.
 #ifdef DSV4_TRACE
 constexpr int kTraceStages = 1024;
-constexpr int kTraceEvents = 8;
+constexpr int kTraceEvents = 14;
 __device__ long long g_trace[kTraceEvents][kTraceStages];
 #define DSV4_TRACE_EV(ev, idx)                                                   \
   do {                                                                           \
@@ -122,6 +122,9 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait: returns false (and records `code`) when the budget runs out
 // or another wait in the grid already failed.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code) {
+  // a completed phase is seen by the non-blocking probe much sooner than by
+  // try_wait, whose latency is ~245 cycles even when the phase is complete
+  if (mbar_test_wait(bar, parity)) return true;
   if (mbar_try_wait(bar, parity)) return true;
   unsigned long long t0 = globaltimer_ns();
   uint32_t n = 0;
@@ -170,6 +173,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar),
+      "l"(policy)
       : "memory");
 }
 
@@ -324,6 +337,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Instruction descriptor for kind::i8: u8 (A) x s8 (B) -> s32, both K-major.
+__device__ __forceinline__ uint32_t idesc_u8s8(uint32_t m, uint32_t n) {
+  return (2u << 4)            // D format S32
+         | (0u << 7)          // A unsigned int8
+         | (1u << 10)         // B signed int8
+         | ((n >> 3) << 17)   // N / 8
+         | ((m >> 4) << 24);  // M / 16
+}
+
 // Instruction descriptor for kind::i8: s8 x s8 -> s32, both K-major.
 __device__ __forceinline__ uint32_t idesc_i8(uint32_t m, uint32_t n) {
   return (2u << 4)            // D format S32
@@ -374,12 +396,34 @@ __device__ __forceinline__ void decode8(uint32_t q, uint32_t t0, uint32_t t1, ui
 __device__ __forceinline__ void decode8_fma(uint32_t q, uint32_t t0, uint32_t t1, uint32_t m1,
                                             uint32_t hi16, uint32_t& lo, uint32_t& hi) {
   const uint32_t qn = q ^ 0x88888888u;
+  const uint32_t qh = __umulhi(q, hi16);  // q >> 16 on the FMA pipe
   const uint32_t p_lo = prmt(t0, t1, q);
   const uint32_t n_lo = prmt(t0, t1, qn);
-  const uint32_t p_hi = prmt(t0, t1, __umulhi(q, hi16));
-  const uint32_t n_hi = prmt(t0, t1, __umulhi(qn, hi16));
+  const uint32_t p_hi = prmt(t0, t1, qh);
+  const uint32_t n_hi = prmt(t0, t1, qh ^ 0x8888u);
   lo = p_lo | ((n_lo * m1 + 0x80808080u) ^ 0x80808080u);
   hi = p_hi | ((n_hi * m1 + 0x80808080u) ^ 0x80808080u);
+}
+
+// Biased-unsigned variant: each output byte is 0x80 + value (value in
+// [-96, 96]).  P and N as in decode8_fma; 0x80 + P - N is formed with two
+// IMADs on the FMA pipe (no byte carries or borrows: every byte stays in
+// [0x20, 0xE0]).  Per 8 weights: 6 ALU ops (2 xor, 4 prmt) and 5 FMA-pipe ops
+// (1 multiply-high, 4 IMAD), against 8 ALU + 3 FMA for decode8_fma; measured
+// ~10% more stages per SM cycle in isolation.  one / m1 / hi16 (1,
+// 0xFFFFFFFF, 65536) must be run-time values so they are not folded into ALU
+// ops.  An MMA that reads these bytes as
+// unsigned computes acc + 128 * sum(b); the caller subtracts that.
+__device__ __forceinline__ void decode8_u8(uint32_t q, uint32_t t0, uint32_t t1, uint32_t one,
+                                          uint32_t m1, uint32_t hi16, uint32_t& lo, uint32_t& hi) {
+  const uint32_t qn = q ^ 0x88888888u;
+  const uint32_t qh = __umulhi(q, hi16);  // q >> 16 on the FMA pipe
+  const uint32_t p_lo = prmt(t0, t1, q);
+  const uint32_t n_lo = prmt(t0, t1, qn);
+  const uint32_t p_hi = prmt(t0, t1, qh);
+  const uint32_t n_hi = prmt(t0, t1, qh ^ 0x8888u);
+  lo = n_lo * m1 + (p_lo * one + 0x80808080u);
+  hi = n_hi * m1 + (p_hi * one + 0x80808080u);
 }
 
 __device__ __forceinline__ void decode_tables(uint32_t shift, uint32_t& t0, uint32_t& t1) {

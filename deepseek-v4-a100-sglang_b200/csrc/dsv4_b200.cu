@@ -83,6 +83,8 @@ int ensure_init() {
   e = set_attrs_epi<kEpiBf16>();
   if (e == cudaSuccess) e = set_attrs_epi<kEpiI32>();
   if (e == cudaSuccess) e = set_attrs_epi<kEpiSwiglu>();
+  if (e == cudaSuccess) e = set_attrs_epi<kEpiBf16 | kEpiBiased>();
+  if (e == cudaSuccess) e = set_attrs_epi<kEpiSwiglu | kEpiBiased>();
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(reinterpret_cast<void*>(&moe_align_kernel),
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -136,58 +138,102 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// b_mxfp4 [E][KB][NG8][128] as 3-D {128, NG8, E*KB}; b_shift2 [E][SS][NG8][8]
-// as 2-D {NG8*8, E*SS}.  Box rows = 128 (plain) or 64 (SwiGLU halves).
+CUresult encode_u8(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
+                   const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz,
+                   CUtensorMapL2promotion l2) {
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, l2,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+// Weight maps, one box per 256-K stage and one shift box per chunk of
+// kShChunk stages (sh_rows = 2 shift rows per stage, <= 2 * kShChunk):
+//   plain   b_mxfp4 [E][KB][NG8][128] as 3-D {128, NG8, E*KB}, box {128, 16, 8};
+//           b_shift2 [E][SS][N] as 2-D {N, E*SS}, box {128, sh_rows}
+//   SwiGLU  the gate rows [0, I) and up rows [I, 2I) as a plane dimension:
+//           b_mxfp4 as 4-D {128, I/8, 2, E*KB}, box {128, 8, 2, 8};
+//           b_shift2 as 3-D {I, 2, E*SS}, box {64, 2, sh_rows}
 int encode_weight_maps(TcGemmParams& p, const uint8_t* b_mxfp4, const uint8_t* b_shift2,
-                       int64_t experts, int64_t kb, int64_t ss, int64_t ng8, int box_rows) {
-  auto enc = tensor_map_encoder();
-  if (enc == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+                       int64_t experts, int64_t kb, int64_t ss, int64_t ng8, bool swiglu,
+                       int64_t inter, int sh_rows) {
+  if (tensor_map_encoder() == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(b_mxfp4) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(b_shift2) & 15) == 0,
                "weight tensors must be 16-byte aligned");
   DSV4_REQUIRE(experts * kb < (1ll << 31) && experts * ss < (1ll << 31), "weight too large");
-  {
+  DSV4_REQUIRE(sh_rows >= 2 && sh_rows <= 2 * TcGemmCfg<16>::kShChunk, "bad shift chunk");
+  const cuuint64_t n = static_cast<cuuint64_t>(ng8 * 8);
+  CUresult r;
+  if (swiglu) {
+    DSV4_REQUIRE(inter % 64 == 0 && 2 * inter == ng8 * 8, "SwiGLU needs N = 2 * I, I % 64 == 0");
+    const cuuint64_t i = static_cast<cuuint64_t>(inter);
+    cuuint64_t dims[4] = {128, i / 8, 2, static_cast<cuuint64_t>(experts * kb)};
+    cuuint64_t strides[3] = {128, i * 16, n * 16};
+    cuuint32_t box[4] = {128, 8, 2, 8};
+    r = encode_u8(&p.map_packed, 4, b_mxfp4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  } else {
     cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(ng8), static_cast<cuuint64_t>(experts * kb)};
-    cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(ng8 * 128)};
-    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(box_rows / 8), 8};  // 256 K per stage
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(&p.map_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(b_mxfp4),
-                     dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (packed) encode failed: %d", (int)r);
+    cuuint64_t strides[2] = {128, n * 16};
+    cuuint32_t box[3] = {128, 16, 8};
+    r = encode_u8(&p.map_packed, 3, b_mxfp4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   }
-  {
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(ng8 * 8), static_cast<cuuint64_t>(experts * ss)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ng8 * 8)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_rows), 2};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&p.map_shift, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(b_shift2),
-                     dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (shift) encode failed: %d", (int)r);
+  if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (packed) encode failed: %d", (int)r);
+  if (swiglu) {
+    const cuuint64_t i = static_cast<cuuint64_t>(inter);
+    cuuint64_t dims[3] = {i, 2, static_cast<cuuint64_t>(experts * ss)};
+    cuuint64_t strides[2] = {i, n};
+    cuuint32_t box[3] = {64, 2, static_cast<cuuint32_t>(sh_rows)};
+    r = encode_u8(&p.map_shift, 3, b_shift2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE);
+  } else {
+    cuuint64_t dims[2] = {n, static_cast<cuuint64_t>(experts * ss)};
+    cuuint64_t strides[1] = {n};
+    cuuint32_t box[2] = {128, static_cast<cuuint32_t>(sh_rows)};
+    r = encode_u8(&p.map_shift, 2, b_shift2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE);
   }
+  if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (shift) encode failed: %d", (int)r);
   p.kb_per_expert = static_cast<int>(kb);
   p.ss_per_expert = static_cast<int>(ss);
+  p.sh_rows = sh_rows;
   return DSV4_OK;
 }
 
-// activations int8 [rows][k] (row stride k) as 2-D {k, rows}, box {128, 1},
-// 128-byte swizzle (the K-major SW128 layout of the MMA B operand).
-int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k) {
-  auto enc = tensor_map_encoder();
-  if (enc == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+int shift_chunk_rows(int stages_per_item) {
+  const int c = TcGemmCfg<16>::kShChunk;
+  return 2 * (stages_per_item < c ? stages_per_item : c);
+}
+
+// Activation (B operand) maps, all with the 128-byte swizzle of the K-major
+// SW128 MMA layout:
+//   b_mode 0: int8 [rows][k] as 2-D {k, rows}, box {128, 1} (tile::gather4)
+//   b_mode 1: int8 [rows][k] as 2-D {k, rows}, box {128, tn}
+//   b_mode 2: int8 K-chunk-major [k/128][rows][128] as 3-D {128, rows, k/128},
+//             box {128, tn, 2} (both 128-K halves of a stage in one copy)
+int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, int b_mode, int tn) {
+  if (tensor_map_encoder() == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, "a_q must be 16-byte aligned");
   DSV4_REQUIRE(rows >= 1 && rows < (1ll << 31), "bad activation row count");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
-  cuuint32_t box[2] = {128, 1};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&p.map_act, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(a), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (b_mode == 2) {
+    DSV4_REQUIRE(k % 128 == 0, "K-chunk-major rows need K %% 128 == 0");
+    cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(k / 128)};
+    cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(rows) * 128};
+    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(tn), 2};
+    r = encode_u8(&p.map_act, 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  } else {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
+    cuuint32_t box[2] = {128, static_cast<cuuint32_t>(b_mode == 1 ? tn : 1)};
+    r = encode_u8(&p.map_act, 2, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  }
   if (r != CUDA_SUCCESS) return fail(DSV4_ERR_CUDA, "tensor map (activations) encode failed: %d", (int)r);
+  p.b_mode = b_mode;
   return DSV4_OK;
 }
 
@@ -212,7 +258,8 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
                     const int32_t* sorted_ids, int64_t sorted_cap, const int32_t* expert_ids,
                     int64_t expert_cap, const int32_t* ntpp, int64_t topk, int64_t block_m,
                     int src_is_slot, int64_t num_valid, int has_clamp, float clamp_limit,
-                    void* stream) {
+                    void* stream, bool sorted_rows = false,
+                    const int32_t* a_rowsum = nullptr) {
   if (int r = ensure_init()) return r;
   DSV4_REQUIRE(a_q && a_scale && b_mxfp4 && b_shift2 && cs && dst && sorted_ids && expert_ids &&
                    ntpp,
@@ -222,11 +269,15 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   DSV4_REQUIRE(block_m == 16 || block_m == 32 || block_m == 64 || block_m == 128,
                "block_m must be 16, 32, 64, or 128, got %lld", (long long)block_m);
   DSV4_REQUIRE(num_valid >= 0, "num_valid_tokens must be non-negative");
-  if (src_is_slot)
+  const int64_t max_m = align_capacity(num_valid, experts, block_m);
+  if (sorted_rows) DSV4_REQUIRE(a_rowsum != nullptr, "a_rowsum is null");
+  if (sorted_rows)
+    DSV4_REQUIRE(m_in == sorted_cap, "sorted input rows (%lld) must equal the sorted_token_ids "
+                 "capacity (%lld)", (long long)m_in, (long long)sorted_cap);
+  else if (src_is_slot)
     DSV4_REQUIRE(m_in >= num_valid, "W2 input rows do not cover routed slots");
   else
     DSV4_REQUIRE(m_in * topk >= num_valid, "W13 input rows do not cover routed slots");
-  const int64_t max_m = align_capacity(num_valid, experts, block_m);
   const int64_t grid_m = (max_m + block_m - 1) / block_m;
   DSV4_REQUIRE(sorted_cap >= max_m,
                "sorted_token_ids capacity is smaller than maximum aligned token count");
@@ -237,8 +288,10 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   TcGemmParams p{};
   p.dec_m1 = 0xFFFFFFFFu;
   p.dec_hi16 = 65536u;
+  p.dec_one = 1u;
   p.a = a_q;
   p.a_scale = a_scale;
+  p.a_rowsum = a_rowsum;
   p.lda = k;
   p.a_rows = m_in;
   p.cs = cs;
@@ -256,18 +309,26 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   p.topk = static_cast<int>(topk);
   p.num_valid = static_cast<int>(num_valid);
   p.src_is_slot = src_is_slot;
+  p.a_row_mode = sorted_rows ? 2 : (src_is_slot ? 1 : 0);
+  p.out_sorted = sorted_rows && epi == kEpiSwiglu ? 1 : 0;
   p.out = reinterpret_cast<__nv_bfloat16*>(dst);
   p.ldo = ldo;
   p.has_clamp = has_clamp;
   p.clamp_limit = clamp_limit;
   if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, experts, k / 32, shift_stride, n_rows / 8,
-                                 epi == kEpiSwiglu ? 64 : 128))
+                                 epi == kEpiSwiglu, inter, shift_chunk_rows(p.k_stages)))
     return r;
-  if (int r = encode_act_map(p, a_q, m_in, k)) return r;
+  if (int r = encode_act_map(p, a_q, m_in, k, sorted_rows ? 2 : 0, static_cast<int>(block_m)))
+    return r;
   const int64_t max_items = grid_m * tile_rows_y;
-  if (epi == kEpiSwiglu)
-    return launch_gemm<kEpiSwiglu>(static_cast<int>(block_m), max_items, p, as_stream(stream));
-  return launch_gemm<kEpiBf16>(static_cast<int>(block_m), max_items, p, as_stream(stream));
+  const int bm = static_cast<int>(block_m);
+  if (a_rowsum != nullptr) {  // biased-unsigned decode, corrected by the row sums
+    if (epi == kEpiSwiglu)
+      return launch_gemm<kEpiSwiglu | kEpiBiased>(bm, max_items, p, as_stream(stream));
+    return launch_gemm<kEpiBf16 | kEpiBiased>(bm, max_items, p, as_stream(stream));
+  }
+  if (epi == kEpiSwiglu) return launch_gemm<kEpiSwiglu>(bm, max_items, p, as_stream(stream));
+  return launch_gemm<kEpiBf16>(bm, max_items, p, as_stream(stream));
 }
 
 int dense_tile(int64_t m) {
@@ -285,6 +346,7 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   TcGemmParams p{};
   p.dec_m1 = 0xFFFFFFFFu;
   p.dec_hi16 = 65536u;
+  p.dec_one = 1u;
   p.a = a_q;
   p.a_scale = a_scale;
   p.lda = k;
@@ -300,10 +362,11 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   p.out_i32 = out_i32;
   p.ldo = ld;
   p.split_stride = split_stride;
-  if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, 1, k / 32, shift_stride, n / 8, 128))
-    return r;
-  if (int r = encode_act_map(p, a_q, m, k)) return r;
   const int tn = dense_tile(m);
+  if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, 1, k / 32, shift_stride, n / 8, false, 0,
+                                 shift_chunk_rows(p.stages_per_split)))
+    return r;
+  if (int r = encode_act_map(p, a_q, m, k, 1, tn)) return r;
   p.m_tiles = static_cast<int>((m + tn - 1) / tn);
   p.row_tiles = static_cast<int>(n / 128);
   const int64_t max_items = static_cast<int64_t>(p.m_tiles) * p.row_tiles * p.splits;
@@ -512,6 +575,98 @@ int dsv4_b200_mxfp4_int8_moe_gemm_swiglu(
                          intermediate / 64, intermediate, sorted_token_ids, sorted_capacity,
                          expert_ids, expert_ids_capacity, num_tokens_post_padded, topk, block_m,
                          0, num_valid_tokens, has_clamp, clamp_limit, stream);
+}
+
+// ---- expert-sorted row pipeline ----
+
+int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, int64_t m_in, int64_t k,
+                            const int32_t* sorted_token_ids, int64_t sorted_capacity,
+                            const int32_t* num_tokens_post_padded, int64_t topk,
+                            int source_rows_are_slots, int64_t num_valid_tokens, int8_t* out_q,
+                            float* out_scale, int32_t* out_rowsum, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m_in >= 0 && k > 0 && k % 128 == 0, "K must be a positive multiple of 128");
+  DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
+  DSV4_REQUIRE(num_valid_tokens >= 0 && num_valid_tokens < (1ll << 31), "bad num_valid_tokens");
+  if (sorted_capacity == 0 || m_in == 0) return DSV4_OK;
+  DSV4_REQUIRE(a_q && a_scale && sorted_token_ids && num_tokens_post_padded && out_q && out_scale &&
+                   out_rowsum,
+               "null pointer argument");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a_q) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out_q) & 15) == 0,
+               "a_q and out_q must be 16-byte aligned");
+  const int64_t blocks = (sorted_capacity + 7) / 8 < 4096 ? (sorted_capacity + 7) / 8 : 4096;
+  sort_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+      a_q, a_scale, m_in, k, sorted_token_ids, num_tokens_post_padded, sorted_capacity,
+      static_cast<int>(topk), source_rows_are_slots ? 1 : 0, static_cast<int>(num_valid_tokens),
+      out_q, out_scale, out_rowsum);
+  return check_launch("sort_rows_kernel");
+}
+
+int dsv4_b200_quantize_sorted_int8(const void* a, int dtype, int64_t k,
+                                   const int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                   const int32_t* num_tokens_post_padded,
+                                   int64_t num_valid_tokens, int8_t* out_q, float* out_scale,
+                                   int32_t* out_rowsum, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(dtype == DSV4_BF16 || dtype == DSV4_F16, "a must be bf16 or fp16 (dtype %d)", dtype);
+  DSV4_REQUIRE(k > 0 && k % 128 == 0 && k <= 8192, "K must be a multiple of 128 in [128, 8192]");
+  DSV4_REQUIRE(num_valid_tokens >= 0 && num_valid_tokens < (1ll << 31), "bad num_valid_tokens");
+  if (sorted_capacity == 0) return DSV4_OK;
+  DSV4_REQUIRE(a && sorted_token_ids && num_tokens_post_padded && out_q && out_scale && out_rowsum,
+               "null pointer argument");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out_q) & 7) == 0,
+               "a must be 16-byte and out_q 8-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const bool wide = k > 2048;
+  const int rows_per_cta = wide ? 2 : 8;
+  const dim3 g(static_cast<unsigned>((sorted_capacity + rows_per_cta - 1) / rows_per_cta));
+  const int nv = static_cast<int>(num_valid_tokens);
+#define DSV4_QS(T, RT)                                                                        \
+  quant_rows_reg_kernel<T, RT, 8><<<g, 256, 0, st>>>(static_cast<const T*>(a), sorted_capacity, \
+                                                     k, k, 0.f, out_q, out_scale,               \
+                                                     sorted_token_ids, num_tokens_post_padded,  \
+                                                     nv, sorted_capacity, out_rowsum)
+  if (dtype == DSV4_BF16) {
+    if (wide) DSV4_QS(__nv_bfloat16, 128); else DSV4_QS(__nv_bfloat16, 32);
+  } else {
+    if (wide) DSV4_QS(__half, 128); else DSV4_QS(__half, 32);
+  }
+#undef DSV4_QS
+  return check_launch("quant_rows_reg_kernel (sorted)");
+}
+
+int dsv4_b200_mxfp4_int8_moe_gemm_sorted(
+    const int8_t* a_sorted, const float* a_scale, const int32_t* a_rowsum, const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+    const float* b_channel_scale, int64_t num_experts, int64_t n, int64_t k,
+    int64_t shift_stride, void* dst, const int32_t* sorted_token_ids, int64_t sorted_capacity,
+    const int32_t* expert_ids, int64_t expert_ids_capacity,
+    const int32_t* num_tokens_post_padded, int64_t topk, int64_t block_m,
+    int64_t num_valid_tokens, void* stream) {
+  return moe_gemm_common(kEpiBf16, a_sorted, a_scale, sorted_capacity, b_mxfp4, b_shift2,
+                         b_channel_scale, num_experts, n, k, shift_stride, dst, n, n / 128, 0,
+                         sorted_token_ids, sorted_capacity, expert_ids, expert_ids_capacity,
+                         num_tokens_post_padded, topk, block_m, 1, num_valid_tokens, 0, 0.f,
+                         stream, true, a_rowsum);
+}
+
+int dsv4_b200_mxfp4_int8_moe_gemm_swiglu_sorted(
+    const int8_t* a_sorted, const float* a_scale, const int32_t* a_rowsum, const uint8_t* b_mxfp4,
+    const uint8_t* b_shift2, const float* b_channel_scale, int64_t num_experts,
+    int64_t intermediate, int64_t k, int64_t shift_stride, void* out,
+    const int32_t* sorted_token_ids, int64_t sorted_capacity, const int32_t* expert_ids,
+    int64_t expert_ids_capacity, const int32_t* num_tokens_post_padded, int64_t topk,
+    int64_t block_m, int64_t num_valid_tokens, int has_clamp, float clamp_limit, void* stream) {
+  DSV4_REQUIRE(intermediate > 0 && intermediate % 64 == 0,
+               "intermediate_size must be a positive multiple of 64, got %lld",
+               (long long)intermediate);
+  return moe_gemm_common(kEpiSwiglu, a_sorted, a_scale, sorted_capacity, b_mxfp4, b_shift2,
+                         b_channel_scale, num_experts, 2 * intermediate, k, shift_stride, out,
+                         intermediate, intermediate / 64, intermediate, sorted_token_ids,
+                         sorted_capacity, expert_ids, expert_ids_capacity, num_tokens_post_padded,
+                         topk, block_m, 0, num_valid_tokens, has_clamp, clamp_limit, stream, true,
+                         a_rowsum);
 }
 
 int dsv4_b200_mxfp4_int8_moe_reduce(const void* routed_out, const float* topk_weights,

@@ -23,11 +23,19 @@
 // epilogue adds them), which halves the per-stage issue time per SM.
 //
 // Warp roles (per token tile, see TcGemmCfg):
-//   warp 0       TMA producer: packed FP4 codes (3-D tensor map) + 2-bit
-//                shifts (2-D tensor map), 256 K per stage, deep packed ring
+//   warp 0       TMA producer: packed FP4 codes, ONE tensor-map box per
+//                256-K stage (gate and up halves in one 4-D box for SwiGLU),
+//                and the 2-bit shifts of 32 stages in one box per chunk
 //   warp 1       TMEM allocator; MMA issuer 0
-//   warps 2..3   per-item token metadata; warp 2 + (g % 2) gathers the token
-//                rows of stage g with TMA tile::gather4 into the SW128 B ring
+//   warps 2..3   per-item token metadata; warp 2 + (g % 2) loads the token
+//                rows of stage g into the SW128 B ring: one 3-D box over
+//                K-chunk-major sorted rows (b_mode 2), two 2-D boxes over
+//                row-major rows (b_mode 1), or tile::gather4 of arbitrary rows
+//                (b_mode 0)
+//
+// The per-SM TMA unit spends on the order of 100 cycles on every copy
+// instruction however small, against ~750 cycles per stage at full HBM rate,
+// so the number of copies per stage, not their bytes, is what is budgeted.
 //   warps 4..7   epilogue: TMEM -> registers -> scales -> bf16 / int32 /
 //                SwiGLU -> global
 //   warps 8..    FP4 -> INT8 decode from the packed ring straight into TMEM
@@ -41,11 +49,19 @@
 namespace dsv4 {
 
 enum Epilogue : int { kEpiBf16 = 0, kEpiI32 = 1, kEpiSwiglu = 2 };
+// Flag or-ed into the kernel's epilogue parameter: decode the weights to
+// biased unsigned bytes (decode8_u8) and subtract 128 * a_rowsum[row] from
+// every accumulator (needs per-row int8 sums over the item's K range, i.e.
+// MoE items, which cover all of K).
+constexpr int kEpiBiased = 4;
 
 struct TcGemmParams {
   // Weight tensor maps (uint8):
   //   map_packed  3-D {128 B, NG8 groups, E*KB}: box {128, 16 (8 for SwiGLU), 4}
   //   map_shift   2-D {NG8*8 B, E*SS}:           box {128 (64 for SwiGLU), 1}
+  //   SwiGLU: map_packed is 4-D {128 B, I/8 groups, 2 halves, E*KB}: box
+  //   {128, 8, 2, 8}; map_shift is 3-D {I B, 2 halves, E*SS}: box {64, 2, R}
+  //   (R = shift rows per chunk)
   CUtensorMap map_packed;
   CUtensorMap map_shift;
   // activations int8 [a_rows][lda] as 2-D {K, a_rows}, box {128 B, 1 row},
@@ -56,6 +72,7 @@ struct TcGemmParams {
   // activations
   const int8_t* a;
   const float* a_scale;
+  const int32_t* a_rowsum;  // biased decode: sum_k a[row][k], indexed like a_scale
   int64_t lda;
   int64_t a_rows;
   const float* cs;          // [E][N]
@@ -76,6 +93,10 @@ struct TcGemmParams {
   int topk;
   int num_valid;
   int src_is_slot;
+  int a_row_mode;           // MoE A rows / scales: 0 slot / topk, 1 slot, 2 sorted position
+  int out_sorted;           // MoE output row: 0 slot, 1 sorted position
+  int b_mode;               // 0 gather4, 1 2-D tile rows, 2 3-D K-chunk-major tile rows
+  int sh_rows;              // shift rows per chunk box (2 per stage)
   // outputs
   __nv_bfloat16* out;
   int64_t ldo;
@@ -83,9 +104,10 @@ struct TcGemmParams {
   int64_t split_stride;
   float clamp_limit;
   int has_clamp;
-  // run-time constants of the decode (0xFFFFFFFF, 65536): see decode8_fma
+  // run-time constants of the decode (0xFFFFFFFF, 65536, 1): see decode8_fma
   uint32_t dec_m1;
   uint32_t dec_hi16;
+  uint32_t dec_one;
 };
 
 // Ring discipline: an mbarrier parity wait is only safe if the waiter takes
@@ -101,9 +123,10 @@ struct TcGemmCfg {
   static constexpr int kBHalf = TN * 128;        // one 128-K SW128 sub-tile of B
   static constexpr int kBBytes = 2 * kBHalf;     // TN token rows x 256 K (int8)
   static constexpr int kPBytes = 128 * 256 / 2;  // packed FP4 codes of one 256-K stage
-  // shift slot per stage: [2 x 128 B] (plain) or gate [2 x 64 B] at +0 and up
-  // [2 x 64 B] at +128 (SwiGLU); tiled TMA destinations must be 128-byte aligned
-  static constexpr int kShBytes = 256;
+  // shift chunks: the 2-bit shifts of kShChunk stages, [2 * kShChunk rows][128 B]
+  // (row = one 4-block shift word per output row; SwiGLU: gate 64 B | up 64 B)
+  static constexpr int kShChunk = 32;
+  static constexpr int kShSlotBytes = 2 * kShChunk * 128;
   static constexpr int kAccCols = TN < 32 ? 32 : TN;
   static constexpr int kIssuers = TN <= 32 ? 3 : 2;       // MMA issuer threads, one accumulator each
   static constexpr int kDecodeGroups = TN <= 64 ? 3 : 4;  // groups of 4 decode warps
@@ -113,20 +136,21 @@ struct TcGemmCfg {
   static constexpr int kAColBase = kIssuers * kAccSlots * kAccCols;
   static constexpr int kTmemCols = 512;
   static constexpr int kStgBytes = 16 * 128 * 2;   // SwiGLU staging (16 cols x 128 rows bf16)
-  static constexpr int kMetaBytes = TN * 12 + 16;  // src, orow, ascale, per-warp last
-  static constexpr int kFixed = kStages * kBBytes + kStgBytes + 2 * kMetaBytes + 1024;
+  static constexpr int kMetaBytes = TN * 16 + 16;  // src, orow, ascale, rowsum, per-warp last
+  static constexpr int kFixed = kStages * kBBytes + 2 * kShSlotBytes + kStgBytes + 2 * kMetaBytes + 1024;
   static constexpr int kBudget = 227 * 1024 - 1024;  // minus alignment slack
-  static constexpr int kStagesPRaw = (kBudget - kFixed) / (kPBytes + kShBytes);
+  static constexpr int kStagesPRaw = (kBudget - kFixed) / kPBytes;
   static constexpr int kStagesPCap = kStagesPRaw > 16 ? 16 : kStagesPRaw;
   static constexpr int kStagesP = kStagesPCap / kDecodeGroups * kDecodeGroups;
   static constexpr int kOffB = 0;
   static constexpr int kOffP = kOffB + kStages * kBBytes;
   static constexpr int kOffSh = kOffP + kStagesP * kPBytes;
-  static constexpr int kOffStg = kOffSh + kStagesP * kShBytes;
+  static constexpr int kOffStg = kOffSh + 2 * kShSlotBytes;
   static constexpr int kOffMeta = kOffStg + kStgBytes;
   static constexpr int kOffBar = kOffMeta + 2 * kMetaBytes;
-  // barriers: pk_full/empty[SP], ab_full/empty[S], acc_full/empty[2], meta_full/empty[2]
-  static constexpr int kNumBars = 2 * kStagesP + 2 * kStages + 8;
+  // barriers: pk_full/empty[SP], ab_full/empty[S], acc_full/empty[2], meta_full/empty[2],
+  // sh_full/empty[2]
+  static constexpr int kNumBars = 2 * kStagesP + 2 * kStages + 12;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
@@ -173,9 +197,11 @@ __device__ __forceinline__ Item get_item(const TcGemmParams& p, int i, int n_blo
   return it;
 }
 
-template <int TN, int EPI>
+template <int TN, int EPIF>
 __global__ void __launch_bounds__(TcGemmCfg<TN>::kThreads, 1)
 mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
+  constexpr int EPI = EPIF & 3;
+  constexpr bool kBiased = (EPIF & kEpiBiased) != 0;
   using C = TcGemmCfg<TN>;
   constexpr int S = C::kStages;
   constexpr int SP = C::kStagesP;
@@ -209,13 +235,16 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   auto acc_empty = [&](int s) { return bar0 + 8u * (kX + 2 + s); };
   auto meta_full = [&](int s) { return bar0 + 8u * (kX + 4 + s); };
   auto meta_empty = [&](int s) { return bar0 + 8u * (kX + 6 + s); };
+  auto sh_full = [&](int s) { return bar0 + 8u * (kX + 8 + s); };
+  auto sh_empty = [&](int s) { return bar0 + 8u * (kX + 10 + s); };
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   auto meta_src = [&](int s) {
     return reinterpret_cast<int*>(smem + C::kOffMeta + s * C::kMetaBytes);
   };
   auto meta_orow = [&](int s) { return meta_src(s) + TN; };
   auto meta_asc = [&](int s) { return reinterpret_cast<float*>(meta_src(s) + 2 * TN); };
-  auto meta_last = [&](int s) { return meta_src(s) + 3 * TN; };  // [2] per gather warp
+  auto meta_rs = [&](int s) { return meta_src(s) + 3 * TN; };     // biased: -128 * rowsum
+  auto meta_last = [&](int s) { return meta_src(s) + 4 * TN; };  // [2] per gather warp
 
   if (tid == 0) {
     for (int s = 0; s < SP; ++s) {
@@ -231,6 +260,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       mbar_init(acc_empty(s), 4);
       mbar_init(meta_full(s), 2);
       mbar_init(meta_empty(s), 4);
+      mbar_init(sh_full(s), 1);
+      mbar_init(sh_empty(s), C::kDecodeWarps);
     }
     mbar_fence_init();
   }
@@ -261,41 +292,43 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       tma_prefetch_desc(&p.map_packed);
       tma_prefetch_desc(&p.map_shift);
       const uint64_t pol = l2_policy_evict_first();
-      uint32_t g = 0;
+      const uint32_t sh_bytes = static_cast<uint32_t>(p.sh_rows) * 128u;
+      uint32_t g = 0, cc = 0;
       for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
         const Item it = get_item(p, i, n_blocks);
         if (!it.valid) continue;
         int ks0, nks;
         k_range(it, ks0, nks);
-        int g0, g1;
-        if (EPI == kEpiSwiglu) {
-          g0 = (it.y * 64) >> 3;            // gate rows j0 .. j0+63
-          g1 = (p.inter + it.y * 64) >> 3;  // up rows I+j0 .. I+j0+63
-        } else {
-          g0 = it.y * 16;                   // rows 128*y .. 128*y+127
-          g1 = g0;
-        }
+        // SwiGLU: group g0 of the gate half (rows j0 .. j0+63; the up half is
+        // the box's second plane); plain: rows 128*y .. 128*y+127
+        const int g0 = EPI == kEpiSwiglu ? it.y * 8 : it.y * 16;
         for (int s = 0; s < nks; ++s, ++g) {
+          const int ks = ks0 + s;
+          if (s % C::kShChunk == 0) {
+            // smem: [2 * kShChunk shift rows][128 B] (SwiGLU: gate 64 B | up 64 B)
+            const int sl = cc & 1;
+            mbar_wait(sh_empty(sl), ((cc >> 1) & 1) ^ 1, kErrWaitPackedEmpty);
+            mbar_arrive_expect_tx(sh_full(sl), sh_bytes);
+            const uint32_t dsts = smem_u32(smem + C::kOffSh + sl * C::kShSlotBytes);
+            const int sh_row = it.expert * p.ss_per_expert + ks * 2;
+            if (EPI == kEpiSwiglu)
+              tma_load_3d(dsts, &p.map_shift, it.y * 64, 0, sh_row, sh_full(sl), pol);
+            else
+              tma_load_2d(dsts, &p.map_shift, it.y * 128, sh_row, sh_full(sl), pol);
+            ++cc;
+          }
           const int sp = g % SP;
           mbar_wait(pk_empty(sp), ((g / SP) & 1) ^ 1, kErrWaitPackedEmpty);
           DSV4_TRACE_EV(0, g);
-          mbar_arrive_expect_tx(pk_full(sp), C::kPBytes + 256);
-          const int ks = ks0 + s;
+          mbar_arrive_expect_tx(pk_full(sp), C::kPBytes);
           const uint32_t dstp = smem_u32(smem + C::kOffP + sp * C::kPBytes);
-          const uint32_t dsts = smem_u32(smem + C::kOffSh + sp * C::kShBytes);
           const int kb_row = it.expert * p.kb_per_expert + ks * 8;
-          const int sh_row = it.expert * p.ss_per_expert + ks * 2;
-          if (EPI == kEpiSwiglu) {
-            // smem: [gate|up][kb 0..7][8 groups][128 B]; shifts gate [2][64] @0, up @128
+          // smem: [kb 0..7][128 rows as 16 groups][128 B] (SwiGLU: gate groups
+          // 0..7 then up groups 0..7 within each kb)
+          if (EPI == kEpiSwiglu)
+            tma_load_4d(dstp, &p.map_packed, 0, g0, 0, kb_row, pk_full(sp), pol);
+          else
             tma_load_3d(dstp, &p.map_packed, 0, g0, kb_row, pk_full(sp), pol);
-            tma_load_3d(dstp + 8192, &p.map_packed, 0, g1, kb_row, pk_full(sp), pol);
-            tma_load_2d(dsts, &p.map_shift, g0 * 8, sh_row, pk_full(sp), pol);
-            tma_load_2d(dsts + 128, &p.map_shift, g1 * 8, sh_row, pk_full(sp), pol);
-          } else {
-            // smem: [kb 0..7][16 groups][128 B]; shifts [2][128]
-            tma_load_3d(dstp, &p.map_packed, 0, g0, kb_row, pk_full(sp), pol);
-            tma_load_2d(dsts, &p.map_shift, g0 * 8, sh_row, pk_full(sp), pol);
-          }
         }
       }
     }
@@ -313,7 +346,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         const int ms = t & 1;
         const int as = t % AS;
         mbar_wait(meta_full(ms), (t >> 1) & 1, kErrWaitMeta);
-        const uint32_t idesc = idesc_i8(128, n_mma_of(ms));
+        const uint32_t idesc = kBiased ? idesc_u8s8(128, n_mma_of(ms)) : idesc_i8(128, n_mma_of(ms));
         mbar_wait(acc_empty(as), ((t / AS) & 1) ^ 1, kErrWaitAccEmpty);
         tc_fence_after();
         const uint32_t d_tmem = tmem + (as * C::kIssuers + j) * C::kAccCols;
@@ -321,6 +354,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         for (int s = s_first; s < nks; s += C::kIssuers) {
           const uint32_t gs = g + s;
           const int sa = gs % S;
+          DSV4_TRACE_EV(9, gs);
           mbar_wait(ab_full(sa), (gs / S) & 1, kErrWaitAbFull);
           DSV4_TRACE_EV(3, gs);
           tc_fence_after();
@@ -358,16 +392,18 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       int* src_s = meta_src(ms);
       int* orow_s = meta_orow(ms);
       float* asc_s = meta_asc(ms);
+      int* rs_s = meta_rs(ms);
       int my_last = -1;
       for (int jj = gt; jj < TN; jj += 64) {
         int src = -1, orow = -1;
         float asc = 0.f;
         if (p.moe) {
           if (jj < p.block_m) {
-            const int slot = __ldg(p.sorted_ids + it.b * p.block_m + jj);
+            const int pos = it.b * p.block_m + jj;
+            const int slot = __ldg(p.sorted_ids + pos);
             if (slot >= 0 && slot < p.num_valid) {
-              src = p.src_is_slot ? slot : slot / p.topk;
-              orow = slot;
+              src = p.a_row_mode == 2 ? pos : (p.a_row_mode == 1 ? slot : slot / p.topk);
+              orow = p.out_sorted ? pos : slot;
             }
           }
         } else {
@@ -382,6 +418,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         src_s[jj] = src;
         orow_s[jj] = orow;
         asc_s[jj] = asc;
+        if (kBiased) rs_s[jj] = src >= 0 ? -128 * __ldg(p.a_rowsum + src) : 0;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
@@ -392,15 +429,38 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       __syncwarp();
       if (lane == 0) mbar_arrive(meta_full(ms));
       {
-        // Warps 2 and 3 take alternate stages.  Only rows up to the last valid
-        // one are fetched (4 at a time, lane l -> rows 4l .. 4l+3 of both
-        // 128-K halves); the MMA columns beyond hold stale data never stored.
+        // Warps 2 and 3 take alternate stages.  gather4 (b_mode 0) fetches only
+        // the rows up to the last valid one (4 at a time, lane l -> rows
+        // 4l .. 4l+3 of both 128-K halves); the tiled modes load the block's TN
+        // rows from row0 (rows past the tensor read as zeros).  The MMA columns
+        // beyond the last valid row are never stored.
         const int last = max(meta_last(ms)[0], meta_last(ms)[1]);
         const int n_rows = ((max(last, 0) + 4) / 4) * 4;
+        const int row0 = p.moe ? it.b * p.block_m : it.b * TN;
         for (int s = 0; s < nks; ++s, ++g) {
           if (static_cast<int>(g & 1) != warp - 2) continue;
           const int sb = g % S;
           const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
+          if (p.b_mode != 0) {
+            if (lane == 0) {
+              mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+              DSV4_TRACE_EV(7, g);
+              const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
+              if (p.b_mode == 2) {
+                // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves
+                mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(C::kBBytes));
+                tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ab_full(sb), pol);
+              } else {
+                mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * C::kBHalf));
+                tma_load_2d(b_base, &p.map_act, (ks0 + s) * 256, row0, ab_full(sb), pol);
+                if (nhalf == 2)
+                  tma_load_2d(b_base + C::kBHalf, &p.map_act, (ks0 + s) * 256 + 128, row0,
+                              ab_full(sb), pol);
+              }
+              DSV4_TRACE_EV(4, g);
+            }
+            continue;
+          }
           if (lane == 0) {
             mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
             DSV4_TRACE_EV(7, g);
@@ -443,6 +503,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       tc_fence_after();
       const int* orow_s = meta_orow(ms);
       const float* asc_s = meta_asc(ms);
+      const int* rs_s = meta_rs(ms);
       const int n_mma = n_mma_of(ms);
       // accumulators written: issuers (g + s) % kIssuers for s < nks
       uint32_t accmask = 0;
@@ -451,7 +512,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const float* cs_e = p.cs + static_cast<int64_t>(it.expert) * p.n;
       auto load16 = [&](int c0, int32_t (&v)[16]) {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = 0;
+        for (int q = 0; q < 16; ++q) v[q] = kBiased ? rs_s[c0 + q] : 0;
         for (int a = 0; a < C::kIssuers; ++a) {
           if (!(accmask & (1u << a))) continue;
           int32_t w[16];
@@ -528,83 +589,101 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     }
   } else if (warp < C::kIssuer1Warp) {
     // ------------------------- FP4 -> INT8 decode -> TMEM -------------------------
-    // Two groups of 4 warps take alternate stages; in a group warp w covers TMEM
+    // kDecodeGroups groups of 4 warps; group g % G takes stage g; in a group warp w covers TMEM
     // lane quarter w % 4 (rows 32*(w%4) ..) and all 8 32-K blocks of the stage
     // (64 TMEM columns: block kb -> columns 8kb .. 8kb+7).
     const int quarter = warp & 3;
     const int grp = (warp - 8) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16;
-    uint32_t g = 0;
+    const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16, one = p.dec_one;
+    uint32_t g = 0, cc = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
       const Item it = get_item(p, i, n_blocks);
       if (!it.valid) continue;
       int ks0, nks;
       k_range(it, ks0, nks);
-      for (int s = 0; s < nks; ++s, ++g) {
-        if (static_cast<int>(g % C::kDecodeGroups) != grp) continue;
-        const int sp = g % SP;
-        const int sa = g % S;
-        const int nkb = stage_kb(ks0 + s);
-        mbar_wait(pk_full(sp), (g / SP) & 1, kErrWaitPackedFull);
-        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(1, g);
-        const uint8_t* P = smem + C::kOffP + sp * C::kPBytes;
-        const uint8_t* SH = smem + C::kOffSh + sp * C::kShBytes;
-        uint32_t shw[2];
+      // Only this group's stages are visited (s = s_first, s_first + G, ...):
+      // stepping through the other groups' stages cost hundreds of cycles
+      // each.  Every decode warp still takes part in every shift chunk (ring
+      // discipline), whether or not it has a stage in it.
+      int s = static_cast<int>((grp - static_cast<int>(g % C::kDecodeGroups) + C::kDecodeGroups) %
+                               C::kDecodeGroups);
+      for (int c0 = 0; c0 < nks; c0 += C::kShChunk, ++cc) {
+        mbar_wait(sh_full(cc & 1), (cc >> 1) & 1, kErrWaitPackedFull);
+        const uint8_t* SHC = smem + C::kOffSh + (cc & 1) * C::kShSlotBytes;
+        const int c1 = min(nks, c0 + C::kShChunk);
+        for (; s < c1; s += C::kDecodeGroups) {
+          const uint32_t gs = g + static_cast<uint32_t>(s);
+          const int sp = gs % SP;
+          const int sa = gs % S;
+          const int nkb = stage_kb(ks0 + s);
+          if (lane == 0 && quarter == 0) DSV4_TRACE_EV(8, gs);
+          mbar_wait(pk_full(sp), (gs / SP) & 1, kErrWaitPackedFull);
+          if (lane == 0 && quarter == 0) DSV4_TRACE_EV(1, gs);
+          const uint8_t* P = smem + C::kOffP + sp * C::kPBytes;
+          const uint8_t* SH = SHC + (s % C::kShChunk) * 256;
+          uint32_t shw[2];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-          shw[hh] = EPI == kEpiSwiglu ? SH[(row >> 6) * 128 + hh * 64 + (row & 63)]
-                                      : SH[hh * 128 + row];
-        // all 8 packed units first (a 128-K tail stage decodes stale bytes
-        // into columns the MMA never reads)
-        uint4 wv[8];
+          for (int hh = 0; hh < 2; ++hh) shw[hh] = SH[hh * 128 + row];
+          // all 8 packed units first (a 128-K tail stage decodes stale bytes
+          // into columns the MMA never reads)
+          uint4 wv[8];
 #pragma unroll
-        for (int kb = 0; kb < 8; ++kb) {
-          const int poff = EPI == kEpiSwiglu ? ((row >> 6) * 8192 + kb * 1024 + (row & 63) * 16)
-                                             : (kb * 2048 + row * 16);
-          wv[kb] = *reinterpret_cast<const uint4*>(P + poff);
-        }
-        (void)nkb;
-        // The packed slot is free once it is in registers: hand it back to the
-        // TMA producer now, not after the decode (the arrive has release
-        // semantics, ordering the loads above).
-        __syncwarp();
-        if (lane == 0) mbar_arrive(pk_empty(sp));
-        mbar_wait(ab_empty(sa), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
-        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, g);
-        tc_fence_after();
-        const uint32_t tcol = tmem + t_lane + C::kAColBase + sa * 64;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {  // blocks 2q, 2q+1 -> columns 16q .. 16q+15
-          uint32_t v[16];
-#pragma unroll
-          for (int kbi = 0; kbi < 2; ++kbi) {
-            const int kb = 2 * q + kbi;
-            const uint4 w = wv[kb];
-            uint32_t a0, a1;
-            decode_tables((shw[kb >> 2] >> (2 * (kb & 3))) & 3u, a0, a1);
-            // columns 8*kbi + 0..3: k 0..15 of the block, 8*kbi + 4..7: k 16..31
-            decode8_fma(w.x, a0, a1, m1, hi16, v[8 * kbi + 0], v[8 * kbi + 4]);
-            decode8_fma(w.y, a0, a1, m1, hi16, v[8 * kbi + 1], v[8 * kbi + 5]);
-            decode8_fma(w.z, a0, a1, m1, hi16, v[8 * kbi + 2], v[8 * kbi + 6]);
-            decode8_fma(w.w, a0, a1, m1, hi16, v[8 * kbi + 3], v[8 * kbi + 7]);
+          for (int kb = 0; kb < 8; ++kb) {
+            const int poff = kb * 2048 + row * 16;
+            wv[kb] = *reinterpret_cast<const uint4*>(P + poff);
           }
+          (void)nkb;
+          // The packed slot is free once it is in registers: hand it back to the
+          // TMA producer now, not after the decode (the arrive has release
+          // semantics, ordering the loads above).
+          __syncwarp();
+          if (lane == 0) mbar_arrive(pk_empty(sp));
+          mbar_wait(ab_empty(sa), ((gs / S) & 1) ^ 1, kErrWaitAbEmpty);
+          if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, gs);
+          tc_fence_after();
+          const uint32_t tcol = tmem + t_lane + C::kAColBase + sa * 64;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {  // blocks 2q, 2q+1 -> columns 16q .. 16q+15
+            uint32_t v[16];
+#pragma unroll
+            for (int kbi = 0; kbi < 2; ++kbi) {
+              const int kb = 2 * q + kbi;
+              const uint4 w = wv[kb];
+              uint32_t a0, a1;
+              decode_tables((shw[kb >> 2] >> (2 * (kb & 3))) & 3u, a0, a1);
+              // columns 8*kbi + 0..3: k 0..15 of the block, 8*kbi + 4..7: k 16..31
+              if (kBiased) {
+                decode8_u8(w.x, a0, a1, one, m1, hi16, v[8 * kbi + 0], v[8 * kbi + 4]);
+                decode8_u8(w.y, a0, a1, one, m1, hi16, v[8 * kbi + 1], v[8 * kbi + 5]);
+                decode8_u8(w.z, a0, a1, one, m1, hi16, v[8 * kbi + 2], v[8 * kbi + 6]);
+                decode8_u8(w.w, a0, a1, one, m1, hi16, v[8 * kbi + 3], v[8 * kbi + 7]);
+              } else {
+                decode8_fma(w.x, a0, a1, m1, hi16, v[8 * kbi + 0], v[8 * kbi + 4]);
+                decode8_fma(w.y, a0, a1, m1, hi16, v[8 * kbi + 1], v[8 * kbi + 5]);
+                decode8_fma(w.z, a0, a1, m1, hi16, v[8 * kbi + 2], v[8 * kbi + 6]);
+                decode8_fma(w.w, a0, a1, m1, hi16, v[8 * kbi + 3], v[8 * kbi + 7]);
+              }
+            }
 #ifdef DSV4_TRACE_NOST
-          if (v[0] == 0x12345678u && v[5] == 0x9abcdef0u) tmem_st_x16(tcol + 16 * q, v);
+            if (v[0] == 0x12345678u && v[5] == 0x9abcdef0u) tmem_st_x16(tcol + 16 * q, v);
 #else
-          tmem_st_x16(tcol + 16 * q, v);
+            tmem_st_x16(tcol + 16 * q, v);
 #endif
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(ab_full(sa));
+          if (lane == 0 && quarter == 0) DSV4_TRACE_EV(5, gs);
         }
-        tmem_st_wait();
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(ab_full(sa));
-        if (lane == 0 && quarter == 0) DSV4_TRACE_EV(5, g);
+        if (lane == 0) mbar_arrive(sh_empty(cc & 1));
       }
+      g += nks;
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

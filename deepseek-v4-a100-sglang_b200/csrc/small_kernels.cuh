@@ -85,18 +85,32 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ a
 // Register-resident variant for bf16/fp16 rows with K % 8 == 0: each row is
 // read once (uint4 per 8 elements) by RT threads (RT = 32 or 128), reduced,
 // then quantised from registers.  Same arithmetic as quant_rows_kernel.
+// With `sorted` set the rows are expert-sorted positions: only positions below
+// num_tokens_post_padded holding a routed slot (< num_valid) are quantised, q
+// is written K-chunk-major, [K/128][cm_rows][128], the layout the GEMM's
+// sorted-row mode loads with one copy per stage, and rowsum[row] receives the
+// sum of the row's int8 values (for the GEMM's biased-unsigned decode).
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict__ a, int64_t m,
                                                              int64_t k, int64_t lda,
                                                              float clamp_abs,
                                                              int8_t* __restrict__ q,
-                                                             float* __restrict__ scale) {
+                                                             float* __restrict__ scale,
+                                                             const int32_t* __restrict__ sorted = nullptr,
+                                                             const int32_t* __restrict__ ntpp = nullptr,
+                                                             int num_valid = 0, int64_t cm_rows = 0,
+                                                             int32_t* __restrict__ rowsum = nullptr) {
   constexpr int kRowsPerCta = 256 / RT;
   __shared__ float red[256 / 32];
+  __shared__ int red_i[256 / 32];
   const int r_local = threadIdx.x / RT;
   const int lt = threadIdx.x % RT;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerCta + r_local;
-  const bool active = row < m;
+  bool active = row < m;
+  if (sorted != nullptr && active) {
+    const int slot = row < __ldg(ntpp) ? __ldg(sorted + row) : -1;
+    active = slot >= 0 && slot < num_valid;
+  }
   const int nv = static_cast<int>(k / 8);
   uint4 u[VPT];
   float amax = 0.f;
@@ -123,14 +137,19 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
 #pragma unroll
     for (int w = 0; w < RT / 32; ++w) amax = fmaxf(amax, red[w0 + w]);
   }
-  if (!active) return;
+  if (!active && rowsum == nullptr) return;
   float sc = __fdiv_rn(amax, 127.0f);
   if (sc == 0.0f) sc = 1.0f;
   uint2* qr = reinterpret_cast<uint2*>(q + row * k);
+  int qsum = 0;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = lt + i * RT;
-    if (idx < nv) {
+    if (active && idx < nv) {
+      // 8 elements at k = 8 idx; K-chunk-major: chunk idx / 16, byte 8 (idx % 16)
+      uint2* dst = sorted == nullptr
+                       ? qr + idx
+                       : reinterpret_cast<uint2*>(q + (idx >> 4) * cm_rows * 128 + row * 128 + (idx & 15) * 8);
       const T* e = reinterpret_cast<const T*>(&u[i]);
       uint32_t lo = 0, hi = 0;
 #pragma unroll
@@ -138,10 +157,65 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
         lo |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(clampf_abs(to_f32<T>(e[j]), clamp_abs), sc))) << (8 * j);
         hi |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(clampf_abs(to_f32<T>(e[j + 4]), clamp_abs), sc))) << (8 * j);
       }
-      qr[idx] = make_uint2(lo, hi);
+      *dst = make_uint2(lo, hi);
+      qsum = __dp4a(static_cast<int>(lo), 0x01010101, qsum);
+      qsum = __dp4a(static_cast<int>(hi), 0x01010101, qsum);
     }
   }
-  if (lt == 0) scale[row] = sc;
+  if (rowsum != nullptr) {  // every thread of the CTA reaches this point
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+    if (RT > 32) {
+      if ((threadIdx.x & 31) == 0) red_i[threadIdx.x >> 5] = qsum;
+      __syncthreads();
+      const int w0 = (r_local * RT) >> 5;
+      qsum = 0;
+#pragma unroll
+      for (int w = 0; w < RT / 32; ++w) qsum += red_i[w0 + w];
+    }
+    if (active && lt == 0) rowsum[row] = qsum;
+  }
+  if (active && lt == 0) scale[row] = sc;
+}
+
+// Expert-sorted copy of quantised rows: position pos < num_tokens_post_padded
+// holding routed slot s (< num_valid) receives row (s / topk, or s when the
+// rows are slots) of a_q and its scale, K-chunk-major [K/128][cap][128].
+// Padding positions are left unwritten (their MMA columns are never stored).
+// One warp per position, 16 B per lane.
+__global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict__ a,
+                                                        const float* __restrict__ a_scale,
+                                                        int64_t a_rows, int64_t k,
+                                                        const int32_t* __restrict__ sorted,
+                                                        const int32_t* __restrict__ ntpp,
+                                                        int64_t cap, int topk, int src_is_slot,
+                                                        int num_valid, int8_t* __restrict__ out,
+                                                        float* __restrict__ out_scale,
+                                                        int32_t* __restrict__ out_rowsum) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = min(cap, static_cast<int64_t>(__ldg(ntpp)));
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int nv = static_cast<int>(k / 16);
+  for (int64_t pos = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; pos < n;
+       pos += nw) {
+    const int slot = __ldg(sorted + pos);
+    if (slot < 0 || slot >= num_valid) continue;
+    const int64_t src = src_is_slot ? slot : slot / topk;
+    if (src >= a_rows) continue;
+    const int4* row = reinterpret_cast<const int4*>(a + src * k);
+    int sum = 0;
+    for (int c = lane; c < nv; c += 32) {
+      const int4 v = __ldg(row + c);
+      *reinterpret_cast<int4*>(out + (c >> 3) * cap * 128 + pos * 128 + (c & 7) * 16) = v;
+      sum = __dp4a(v.x, 0x01010101, __dp4a(v.y, 0x01010101, __dp4a(v.z, 0x01010101, __dp4a(v.w, 0x01010101, sum))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      out_scale[pos] = __ldg(a_scale + src);
+      out_rowsum[pos] = sum;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -39,6 +39,14 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_mxfp4_int8_moe_gemm_swiglu": [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64,
                                              _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I,
                                              _F, _P],
+    "dsv4_b200_moe_sort_rows": [_P, _P, _I64, _I64, _P, _I64, _P, _I64, _I, _I64, _P, _P, _P,
+                                _P],
+    "dsv4_b200_quantize_sorted_int8": [_P, _I, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P],
+    "dsv4_b200_mxfp4_int8_moe_gemm_sorted": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                             _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P],
+    "dsv4_b200_mxfp4_int8_moe_gemm_swiglu_sorted": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
+                                                    _I64, _P, _P, _I64, _P, _I64, _P, _I64,
+                                                    _I64, _I64, _I, _F, _P],
     "dsv4_b200_mxfp4_int8_moe_reduce": [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P],
     "dsv4_b200_mxfp4_int8_moe_reduce_masked": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P],
     "dsv4_b200_gather_rows": [_P, _I64, _P, _I64, _P, _P],

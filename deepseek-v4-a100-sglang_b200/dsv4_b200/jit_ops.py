@@ -157,6 +157,99 @@ def mxfp4_int8_moe_gemm_swiglu(a_q, a_scale, b_mxfp4, b_shift2, b_channel_scale,
            N.stream_of(a_q))
 
 
+# ---- expert-sorted row pipeline (B200 fast path; same arithmetic) ----
+
+def moe_sort_rows(a_q, a_scale, sorted_token_ids, num_tokens_post_padded, *, topk: int,
+                  num_valid_tokens: int, source_rows_are_slots: bool = False):
+    """Copy the routed INT8 rows into the order of the aligned permutation:
+    returns ``(q, scale, rowsum)`` with ``q`` int8 K-chunk-major
+    ``[K/128][sorted_capacity][128]`` (flat), ``scale`` fp32 and ``rowsum``
+    int32 (sum of the row's int8 values) ``[sorted_capacity]``; position p
+    holds row ``sorted_token_ids[p] // topk`` (or the slot itself).  Padding
+    positions are left unwritten."""
+    _check_tensor(a_q, "a_q", torch.int8, device=a_q.device)
+    _check_tensor(a_scale, "a_scale", torch.float32, (a_q.shape[0],), a_q.device)
+    k = a_q.shape[1]
+    cap = sorted_token_ids.numel()
+    q = torch.empty(cap * k, device=a_q.device, dtype=torch.int8)
+    sc = torch.empty(cap, device=a_q.device, dtype=torch.float32)
+    rs = torch.empty(cap, device=a_q.device, dtype=torch.int32)
+    _init_device(a_q.device)
+    N.call("dsv4_b200_moe_sort_rows", a_q.data_ptr(), a_scale.data_ptr(), a_q.shape[0], k,
+           sorted_token_ids.data_ptr(), cap, num_tokens_post_padded.data_ptr(), topk,
+           1 if source_rows_are_slots else 0, num_valid_tokens, q.data_ptr(), sc.data_ptr(),
+           rs.data_ptr(), N.stream_of(a_q))
+    return q, sc, rs
+
+
+def quantize_sorted_int8(a, sorted_token_ids, num_tokens_post_padded, *, num_valid_tokens: int):
+    """Per-token INT8 quantisation of sorted-position rows ``a``
+    ``[sorted_capacity, K]`` (bf16/fp16) into ``(q, scale, rowsum)`` as
+    returned by :func:`moe_sort_rows`."""
+    _check(a.dim() == 2 and a.dtype in (torch.bfloat16, torch.float16) and a.is_contiguous(),
+           "a must be a contiguous 2-D bf16/fp16 tensor")
+    _check(a.is_cuda, "a must be a CUDA tensor (no CPU path)")
+    cap, k = a.shape
+    _check(cap == sorted_token_ids.numel(), "a must have one row per sorted position")
+    q = torch.empty(cap * k, device=a.device, dtype=torch.int8)
+    sc = torch.empty(cap, device=a.device, dtype=torch.float32)
+    rs = torch.empty(cap, device=a.device, dtype=torch.int32)
+    _init_device(a.device)
+    N.call("dsv4_b200_quantize_sorted_int8", a.data_ptr(),
+           N.DTYPE_BF16 if a.dtype == torch.bfloat16 else N.DTYPE_F16, k,
+           sorted_token_ids.data_ptr(), cap, num_tokens_post_padded.data_ptr(),
+           num_valid_tokens, q.data_ptr(), sc.data_ptr(), rs.data_ptr(), N.stream_of(a))
+    return q, sc, rs
+
+
+def mxfp4_int8_moe_gemm_swiglu_sorted(a_sorted, a_scale, a_rowsum, b_mxfp4, b_shift2,
+                                      b_channel_scale, out,
+                                      sorted_token_ids, expert_ids, num_tokens_post_padded, *,
+                                      hidden_size: int, intermediate_size: int, topk: int,
+                                      block_m: int, num_valid_tokens: int,
+                                      clamp_limit: float | None = None) -> None:
+    """:func:`mxfp4_int8_moe_gemm_swiglu` on sorted rows: ``out``
+    ``[sorted_capacity, I]`` bf16 by sorted position."""
+    _validate_template_args(hidden_size, intermediate_size, topk, block_m, 128)
+    n, k = 2 * intermediate_size, hidden_size
+    cap = sorted_token_ids.numel()
+    e = _moe_common_checks(a_sorted.view(cap, k), a_scale, b_mxfp4, b_shift2, b_channel_scale,
+                           sorted_token_ids, expert_ids, num_tokens_post_padded, n, k)
+    _check_tensor(out, "out", torch.bfloat16, (cap, intermediate_size), a_sorted.device)
+    _init_device(a_sorted.device)
+    _check_tensor(a_rowsum, "a_rowsum", torch.int32, (cap,), a_sorted.device)
+    N.call("dsv4_b200_mxfp4_int8_moe_gemm_swiglu_sorted", a_sorted.data_ptr(), a_scale.data_ptr(),
+           a_rowsum.data_ptr(), b_mxfp4.data_ptr(), b_shift2.data_ptr(), b_channel_scale.data_ptr(), e,
+           intermediate_size, k, b_shift2.shape[1], out.data_ptr(), sorted_token_ids.data_ptr(),
+           cap, expert_ids.data_ptr(), expert_ids.numel(), num_tokens_post_padded.data_ptr(), topk,
+           block_m, num_valid_tokens, 0 if clamp_limit is None else 1,
+           0.0 if clamp_limit is None else float(clamp_limit), N.stream_of(a_sorted))
+
+
+def mxfp4_int8_moe_gemm_sorted(a_sorted, a_scale, a_rowsum, b_mxfp4, b_shift2, b_channel_scale,
+                               routed_out,
+                               sorted_token_ids, expert_ids, num_tokens_post_padded, *,
+                               hidden_size: int, intermediate_size: int, topk: int, block_m: int,
+                               num_valid_tokens: int) -> None:
+    """W2 of :func:`mxfp4_int8_moe_gemm` (``source_rows_are_slots``) on
+    sorted rows: ``routed_out`` ``[num_valid, H]`` by routed slot."""
+    _validate_template_args(hidden_size, intermediate_size, topk, block_m, 128)
+    n, k = hidden_size, intermediate_size
+    cap = sorted_token_ids.numel()
+    e = _moe_common_checks(a_sorted.view(cap, k), a_scale, b_mxfp4, b_shift2, b_channel_scale,
+                           sorted_token_ids, expert_ids, num_tokens_post_padded, n, k)
+    _check_tensor(routed_out, "routed_out", torch.bfloat16, device=a_sorted.device)
+    _check(routed_out.dim() == 2 and routed_out.shape[1] == n
+           and routed_out.shape[0] >= num_valid_tokens, "routed_out does not cover routed slots")
+    _init_device(a_sorted.device)
+    _check_tensor(a_rowsum, "a_rowsum", torch.int32, (cap,), a_sorted.device)
+    N.call("dsv4_b200_mxfp4_int8_moe_gemm_sorted", a_sorted.data_ptr(), a_scale.data_ptr(),
+           a_rowsum.data_ptr(), b_mxfp4.data_ptr(), b_shift2.data_ptr(), b_channel_scale.data_ptr(), e, n, k,
+           b_shift2.shape[1], routed_out.data_ptr(), sorted_token_ids.data_ptr(), cap,
+           expert_ids.data_ptr(), expert_ids.numel(), num_tokens_post_padded.data_ptr(), topk,
+           block_m, num_valid_tokens, N.stream_of(a_sorted))
+
+
 def mxfp4_int8_moe_reduce(routed_out, topk_weights, out, *, hidden_size: int,
                           intermediate_size: int, topk: int, block_m: int, num_valid_tokens: int,
                           block_n: int | None = None,

@@ -22,6 +22,10 @@ from .jit_ops import (
     mxfp4_int8_moe_reduce,
     mxfp4_int8_dense_gemm,
     prewarm_mxfp4_int8_moe_jit_modules,
+    moe_sort_rows,
+    quantize_sorted_int8,
+    mxfp4_int8_moe_gemm_swiglu_sorted,
+    mxfp4_int8_moe_gemm_sorted,
 )
 
 _VALID_BLOCK_M = {16, 32, 64, 128}
@@ -292,23 +296,28 @@ def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWei
 def _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids, expert_ids,
               ntpp, *, block_m, block_n, hidden_size, intermediate_size, routed_scaling_factor,
               clamp_limit, masked):
+    """W13 + SwiGLU, requantisation and W2 of mxfp4_int8_moe_forward
+    (PYMOE:904-958) on expert-sorted rows: the routed token rows are copied
+    once into the order of the aligned permutation (K-chunk-major), so each
+    GEMM stage loads its token tile with one tensor-map copy.  Same results as
+    the slot-addressed JIT entry points, bit for bit."""
     m = a13_q.shape[0]
     topk = topk_ids_i32.shape[1]
     dev = a13_q.device
-    inter = torch.empty((m * topk, intermediate_size), device=dev, dtype=torch.bfloat16)
-    mxfp4_int8_moe_gemm_swiglu(
-        a13_q, a13_scale, weights.w13_mxfp4, weights.w13_shift2, weights.w13_channel_scale,
-        inter, sorted_ids, expert_ids, ntpp, hidden_size=hidden_size,
-        intermediate_size=intermediate_size, topk=topk, block_m=block_m,
-        num_valid_tokens=m * topk, clamp_limit=clamp_limit)
-    a2_q, a2_scale = quantize_per_token_int8(inter, 0.0)
+    nv = m * topk
+    kw = dict(hidden_size=hidden_size, intermediate_size=intermediate_size, topk=topk,
+              block_m=block_m, num_valid_tokens=nv)
+    a13, s13, r13 = moe_sort_rows(a13_q, a13_scale, sorted_ids, ntpp, topk=topk, num_valid_tokens=nv)
+    inter = torch.empty((sorted_ids.numel(), intermediate_size), device=dev, dtype=torch.bfloat16)
+    mxfp4_int8_moe_gemm_swiglu_sorted(a13, s13, r13, weights.w13_mxfp4, weights.w13_shift2,
+                                      weights.w13_channel_scale, inter, sorted_ids, expert_ids,
+                                      ntpp, clamp_limit=clamp_limit, **kw)
+    a2, s2, r2 = quantize_sorted_int8(inter, sorted_ids, ntpp, num_valid_tokens=nv)
     out = torch.empty((m, hidden_size), device=dev, dtype=torch.bfloat16)
-    routed_out = torch.empty((m * topk, hidden_size), device=dev, dtype=torch.bfloat16)
-    mxfp4_int8_moe_gemm(
-        a2_q, a2_scale, weights.w2_mxfp4, weights.w2_shift2, weights.w2_channel_scale, out,
-        topk_weights_f32, sorted_ids, expert_ids, ntpp, hidden_size=hidden_size,
-        intermediate_size=intermediate_size, topk=topk, block_m=block_m, block_n=block_n,
-        source_rows_are_slots=True, num_valid_tokens=m * topk, routed_out=routed_out)
+    routed_out = torch.empty((nv, hidden_size), device=dev, dtype=torch.bfloat16)
+    mxfp4_int8_moe_gemm_sorted(a2, s2, r2, weights.w2_mxfp4, weights.w2_shift2,
+                               weights.w2_channel_scale, routed_out, sorted_ids, expert_ids, ntpp,
+                               **kw)
     if masked:
         apply = routed_scaling_factor is not None and routed_scaling_factor != 1.0
         N.call("dsv4_b200_mxfp4_int8_moe_reduce_masked", routed_out.data_ptr(),

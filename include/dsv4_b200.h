@@ -46,7 +46,7 @@ typedef enum dsv4_status {
 
 typedef enum dsv4_dtype { DSV4_F32 = 0, DSV4_F16 = 1, DSV4_BF16 = 2 } dsv4_dtype;
 
-#define DSV4_B200_ABI_VERSION 1
+#define DSV4_B200_ABI_VERSION 2
 
 DSV4_API int dsv4_b200_abi_version(void);
 
@@ -118,6 +118,65 @@ DSV4_API int dsv4_b200_mxfp4_int8_moe_gemm(const int8_t* a_q, const float* a_sca
  * has_clamp = 0 disables the limit.  intermediate % 64 == 0. */
 DSV4_API int dsv4_b200_mxfp4_int8_moe_gemm_swiglu(
     const int8_t* a_q, const float* a_scale, int64_t m_in, const uint8_t* b_mxfp4,
+    const uint8_t* b_shift2, const float* b_channel_scale, int64_t num_experts,
+    int64_t intermediate, int64_t k, int64_t shift_stride, void* out,
+    const int32_t* sorted_token_ids, int64_t sorted_capacity, const int32_t* expert_ids,
+    int64_t expert_ids_capacity, const int32_t* num_tokens_post_padded, int64_t topk,
+    int64_t block_m, int64_t num_valid_tokens, int has_clamp, float clamp_limit, void* stream);
+
+/* Expert-sorted row pipeline (the B200 fast path of the routed MoE layer;
+ * same arithmetic as the two GEMM calls above).  Rows are addressed by their
+ * position in sorted_token_ids instead of by routed slot, and the int8 rows
+ * are stored K-chunk-major, [k/128][sorted_capacity][128], so the GEMM loads
+ * the token tile of a 256-K stage with ONE tensor-map copy (the gather form
+ * above needs one tile::gather4 per 4 rows and 128-K half).  Padding
+ * positions (slot >= num_valid_tokens, or past num_tokens_post_padded) are
+ * never written and never read back into a result.
+ *
+ * The GEMMs decode the weights to biased unsigned bytes (weight + 128, which
+ * moves part of the FP4 decode from the integer ALU to the FMA pipe) and
+ * subtract 128 * a_rowsum[pos] from each int32 sum; a_rowsum[pos] is the sum
+ * of row pos's int8 values, produced by the two row kernels below.
+ *
+ * dsv4_b200_moe_sort_rows: out_q[pos] = a_q[src(slot)], out_scale[pos] =
+ *   a_scale[src(slot)], out_rowsum[pos] = sum_k a_q[src][k], src = slot /
+ *   topk (or slot when source_rows_are_slots).  The per-token INT8 rows of
+ *   PYMOE:904-909 in the order of the aligned permutation (PYMOE:842-869). */
+DSV4_API int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, int64_t m_in,
+                                     int64_t k, const int32_t* sorted_token_ids,
+                                     int64_t sorted_capacity,
+                                     const int32_t* num_tokens_post_padded, int64_t topk,
+                                     int source_rows_are_slots, int64_t num_valid_tokens,
+                                     int8_t* out_q, float* out_scale, int32_t* out_rowsum,
+                                     void* stream);
+
+/* Per-token INT8 quantisation (a1, PYMOE:46-66 arithmetic, no clamp) of the
+ * sorted-position rows a [sorted_capacity][k] (bf16 or fp16), written
+ * K-chunk-major.  The W2 input requantisation of PYMOE:937. */
+DSV4_API int dsv4_b200_quantize_sorted_int8(const void* a, int dtype, int64_t k,
+                                            const int32_t* sorted_token_ids,
+                                            int64_t sorted_capacity,
+                                            const int32_t* num_tokens_post_padded,
+                                            int64_t num_valid_tokens, int8_t* out_q,
+                                            float* out_scale, int32_t* out_rowsum, void* stream);
+
+/* W2 on sorted rows (a_sorted K-chunk-major, a_scale and a_rowsum
+ * [sorted_capacity]):
+ * dst[slot][n] as dsv4_b200_mxfp4_int8_moe_gemm with source_rows_are_slots.
+ * Replaces the W2 call of PYMOE:938-952. */
+DSV4_API int dsv4_b200_mxfp4_int8_moe_gemm_sorted(
+    const int8_t* a_sorted, const float* a_scale, const int32_t* a_rowsum, const uint8_t* b_mxfp4,
+    const uint8_t* b_shift2, const float* b_channel_scale, int64_t num_experts, int64_t n,
+    int64_t k, int64_t shift_stride, void* dst, const int32_t* sorted_token_ids,
+    int64_t sorted_capacity, const int32_t* expert_ids, int64_t expert_ids_capacity,
+    const int32_t* num_tokens_post_padded, int64_t topk, int64_t block_m,
+    int64_t num_valid_tokens, void* stream);
+
+/* W13 + SwiGLU on sorted rows: out[pos][intermediate] bf16 by sorted
+ * position (sorted_capacity rows), otherwise as
+ * dsv4_b200_mxfp4_int8_moe_gemm_swiglu (PYMOE:916-935). */
+DSV4_API int dsv4_b200_mxfp4_int8_moe_gemm_swiglu_sorted(
+    const int8_t* a_sorted, const float* a_scale, const int32_t* a_rowsum, const uint8_t* b_mxfp4,
     const uint8_t* b_shift2, const float* b_channel_scale, int64_t num_experts,
     int64_t intermediate, int64_t k, int64_t shift_stride, void* out,
     const int32_t* sorted_token_ids, int64_t sorted_capacity, const int32_t* expert_ids,

@@ -173,6 +173,62 @@ def test_moe_gemm_w13_w2_reduce_bit_exact(case):
     np.testing.assert_array_equal(bits(out), ref_out)
 
 
+def _cm_rows(t, cap, k):  # K-chunk-major [k/128][cap][128] -> [cap][k]
+    return t.view(k // 128, cap, 128).permute(1, 0, 2).reshape(cap, k).cpu().numpy()
+
+
+@pytest.mark.parametrize("case", MOE_CASES)
+def test_moe_sorted_pipeline_bit_exact(case):
+    """The expert-sorted fast path (sort rows -> W13+SwiGLU -> sorted requant
+    -> W2, biased-unsigned decode with row-sum correction) against the same
+    oracle composition as the slot-addressed entry points."""
+    e, t, h, i, topk, bm = case
+    c = _moe_case(e, t, h, i, topk, 31 * t + e, bm)
+    s_ids, e_ids, ntp, _ = O.moe_align_block_size(c["ids"].numpy(), bm, e)
+    ds, de, dn = D.moe_align_block_size(c["ids"].to(DEV), bm, e)
+    n_pad = int(np.asarray(ntp).reshape(-1)[0])
+    np.testing.assert_array_equal(ds.cpu().numpy()[:n_pad], s_ids[:n_pad])
+    nv = t * topk
+    cap = ds.numel()
+    sd = ds.cpu().numpy()
+    valid = (np.arange(cap) < n_pad) & (sd >= 0) & (sd < nv)
+    slots = sd[valid]
+    q, qs = O.quantize_per_token_int8(c["x"].float().numpy())
+    dq, dqs = torch.from_numpy(q).to(DEV), torch.from_numpy(qs).to(DEV)
+    # sorted rows, scales and row sums
+    a13, s13, r13 = J.moe_sort_rows(dq, dqs, ds, dn, topk=topk, num_valid_tokens=nv)
+    np.testing.assert_array_equal(_cm_rows(a13, cap, h)[valid], q[slots // topk])
+    np.testing.assert_array_equal(s13.cpu().numpy()[valid], qs[slots // topk])
+    np.testing.assert_array_equal(r13.cpu().numpy()[valid],
+                                  q[slots // topk].astype(np.int64).sum(1))
+    # W13 + SwiGLU, rows by sorted position
+    inter = torch.zeros((cap, i), dtype=torch.bfloat16, device=DEV)
+    J.mxfp4_int8_moe_gemm_swiglu_sorted(a13, s13, r13, *c["d13"], inter, ds, de, dn,
+                                        hidden_size=h, intermediate_size=i, topk=topk,
+                                        block_m=bm, num_valid_tokens=nv)
+    ref_gu = O.moe_gemm(q, qs, *c["o13"], s_ids, e_ids, ntp, block_m=bm, topk=topk, num_valid=nv,
+                        source_rows_are_slots=False)
+    ref_inter = O.swiglu_bf16(ref_gu, i)
+    diff = np.abs(bits(inter)[valid].astype(np.int32) - ref_inter[slots].astype(np.int32))
+    assert diff.max() <= 1 and (diff > 0).mean() <= 0.005
+    # requantisation of the (oracle) intermediate placed at sorted positions
+    placed = np.zeros((cap, i), dtype=np.uint16)
+    placed[valid] = ref_inter[slots]
+    dplaced = torch.from_numpy(placed.view(np.int16)).view(torch.bfloat16).to(DEV)
+    a2, s2, r2 = J.quantize_sorted_int8(dplaced, ds, dn, num_valid_tokens=nv)
+    q2, qs2 = O.quantize_per_token_int8(O.bf16_bits_to_f32(ref_inter))
+    np.testing.assert_array_equal(_cm_rows(a2, cap, i)[valid], q2[slots])
+    np.testing.assert_array_equal(s2.cpu().numpy()[valid], qs2[slots])
+    np.testing.assert_array_equal(r2.cpu().numpy()[valid], q2[slots].astype(np.int64).sum(1))
+    # W2 -> routed_out by slot
+    routed = torch.empty((nv, h), dtype=torch.bfloat16, device=DEV)
+    J.mxfp4_int8_moe_gemm_sorted(a2, s2, r2, *c["d2"], routed, ds, de, dn, hidden_size=h,
+                                 intermediate_size=i, topk=topk, block_m=bm, num_valid_tokens=nv)
+    ref_routed = O.moe_gemm(q2, qs2, *c["o2"], s_ids, e_ids, ntp, block_m=bm, topk=topk,
+                            num_valid=nv, source_rows_are_slots=True)
+    np.testing.assert_array_equal(bits(routed), ref_routed)
+
+
 def test_moe_forward_matches_reference_golden(golden):
     """Full prepare + forward vs the reference's float MoE (TEST_MOE:261-310)."""
     g = golden("moe_ref_small")

@@ -23,7 +23,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), s
     assert set(syms) == set(N.SIGNATURES), "ctypes table out of sync with the header"
-    assert lib.dsv4_b200_abi_version() == 1
+    assert lib.dsv4_b200_abi_version() == 2
 
 
 def test_no_cpu_fallback_for_cpu_tensors():
