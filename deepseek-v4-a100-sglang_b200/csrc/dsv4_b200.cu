@@ -265,6 +265,7 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
                    ntpp,
                "null pointer argument");
   if (int r = check_weights(experts, n_rows, k, shift_stride)) return r;
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(cs) & 15) == 0, "b_channel_scale must be 16-byte aligned");
   DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
   DSV4_REQUIRE(block_m == 16 || block_m == 32 || block_m == 64 || block_m == 128,
                "block_m must be 16, 32, 64, or 128, got %lld", (long long)block_m);
@@ -343,6 +344,8 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
                  const float* cs, int64_t n, void* out, int32_t* out_i32, int64_t splits,
                  int64_t ld, int64_t split_stride, int epi, void* stream) {
   if (int r = check_weights(1, n, k, shift_stride)) return r;
+  DSV4_REQUIRE(cs == nullptr || (reinterpret_cast<uintptr_t>(cs) & 15) == 0,
+               "weight_channel_scale must be 16-byte aligned");
   TcGemmParams p{};
   p.dec_m1 = 0xFFFFFFFFu;
   p.dec_hi16 = 65536u;

@@ -27,11 +27,13 @@
 //                256-K stage (gate and up halves in one 4-D box for SwiGLU),
 //                and the 2-bit shifts of 32 stages in one box per chunk
 //   warp 1       TMEM allocator; MMA issuer 0
-//   warps 2..3   per-item token metadata; warp 2 + (g % 2) loads the token
-//                rows of stage g into the SW128 B ring: one 3-D box over
-//                K-chunk-major sorted rows (b_mode 2), two 2-D boxes over
-//                row-major rows (b_mode 1), or tile::gather4 of arbitrary rows
-//                (b_mode 0)
+//   warps 2..3   token rows of each stage into the SW128 B ring, and the
+//                per-item metadata (rows, scales, channel scales by bulk copy).
+//                Tiled modes: warp 2 metadata, warp 3 one 3-D box per stage
+//                over K-chunk-major sorted rows (b_mode 2) or two 2-D boxes
+//                over row-major rows (b_mode 1).  gather4 mode (b_mode 0):
+//                both warps write metadata, then warp 2 + (g % 2) gathers the
+//                rows of stage g with tile::gather4
 //
 // The per-SM TMA unit spends on the order of 100 cycles on every copy
 // instruction however small, against ~750 cycles per stage at full HBM rate,
@@ -127,17 +129,25 @@ struct TcGemmCfg {
   // (row = one 4-block shift word per output row; SwiGLU: gate 64 B | up 64 B)
   static constexpr int kShChunk = 32;
   static constexpr int kShSlotBytes = 2 * kShChunk * 128;
-  static constexpr int kAccCols = TN < 32 ? 32 : TN;
-  static constexpr int kIssuers = TN <= 32 ? 3 : 2;       // MMA issuer threads, one accumulator each
+  static constexpr int kShSlots = TN <= 64 ? 4 : 2;  // chunks in flight (short-K items: one each)
+  static constexpr int kAccCols = TN;                     // N columns per accumulator
+  // MMA issuer threads, one accumulator each: an issuer sharing its SM
+  // sub-partition with three decode warps issues a 16-token MMA in ~200
+  // cycles, so 16-token tiles (8 MMAs per stage) need three
+  static constexpr int kIssuers = TN <= 16 ? 3 : 2;
   static constexpr int kDecodeGroups = TN <= 64 ? 3 : 4;  // groups of 4 decode warps
-  static constexpr int kAccSlots = 1;                     // accumulator sets (per issuer)
   static constexpr int kStages = TN <= 64 ? 6 : 4;        // A (TMEM, 64 cols) + B (smem) ring
+  // accumulator sets per issuer: two where TMEM has room, so the MMAs of the
+  // next item do not wait for the epilogue of this one
+  static constexpr int kAccSlots = kIssuers * 2 * kAccCols + kStages * 64 <= 512 ? 2 : 1;
   // TMEM (512 columns): [issuer accumulators], then 64-column A slots
   static constexpr int kAColBase = kIssuers * kAccSlots * kAccCols;
   static constexpr int kTmemCols = 512;
   static constexpr int kStgBytes = 16 * 128 * 2;   // SwiGLU staging (16 cols x 128 rows bf16)
-  static constexpr int kMetaBytes = TN * 16 + 16;  // src, orow, ascale, rowsum, per-warp last
-  static constexpr int kFixed = kStages * kBBytes + 2 * kShSlotBytes + kStgBytes + 2 * kMetaBytes + 1024;
+  // src, orow, ascale, rowsum [TN]; per-warp last [4]; channel scales [128]
+  static constexpr int kMetaBytes = TN * 16 + 16 + 512;
+  static constexpr int kMetaSlots = 4;  // items of metadata prepared ahead
+  static constexpr int kFixed = kStages * kBBytes + kShSlots * kShSlotBytes + kStgBytes + kMetaSlots * kMetaBytes + 1024;
   static constexpr int kBudget = 227 * 1024 - 1024;  // minus alignment slack
   static constexpr int kStagesPRaw = (kBudget - kFixed) / kPBytes;
   static constexpr int kStagesPCap = kStagesPRaw > 16 ? 16 : kStagesPRaw;
@@ -145,12 +155,12 @@ struct TcGemmCfg {
   static constexpr int kOffB = 0;
   static constexpr int kOffP = kOffB + kStages * kBBytes;
   static constexpr int kOffSh = kOffP + kStagesP * kPBytes;
-  static constexpr int kOffStg = kOffSh + 2 * kShSlotBytes;
+  static constexpr int kOffStg = kOffSh + kShSlots * kShSlotBytes;
   static constexpr int kOffMeta = kOffStg + kStgBytes;
-  static constexpr int kOffBar = kOffMeta + 2 * kMetaBytes;
-  // barriers: pk_full/empty[SP], ab_full/empty[S], acc_full/empty[2], meta_full/empty[2],
-  // sh_full/empty[2]
-  static constexpr int kNumBars = 2 * kStagesP + 2 * kStages + 12;
+  static constexpr int kOffBar = kOffMeta + kMetaSlots * kMetaBytes;
+  // barriers: pk_full/empty[SP], ab_full/empty[S], acc_full/empty[2],
+  // meta_full/empty[kMetaSlots], sh_full/empty[kShSlots]
+  static constexpr int kNumBars = 2 * kStagesP + 2 * kStages + 4 + 2 * kMetaSlots + 2 * kShSlots;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
@@ -233,10 +243,12 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   constexpr int kX = 2 * SP + 2 * S;
   auto acc_full = [&](int s) { return bar0 + 8u * (kX + s); };
   auto acc_empty = [&](int s) { return bar0 + 8u * (kX + 2 + s); };
+  constexpr int MS = C::kMetaSlots;
   auto meta_full = [&](int s) { return bar0 + 8u * (kX + 4 + s); };
-  auto meta_empty = [&](int s) { return bar0 + 8u * (kX + 6 + s); };
-  auto sh_full = [&](int s) { return bar0 + 8u * (kX + 8 + s); };
-  auto sh_empty = [&](int s) { return bar0 + 8u * (kX + 10 + s); };
+  auto meta_empty = [&](int s) { return bar0 + 8u * (kX + 4 + MS + s); };
+  constexpr int SHS = C::kShSlots;
+  auto sh_full = [&](int s) { return bar0 + 8u * (kX + 4 + 2 * MS + s); };
+  auto sh_empty = [&](int s) { return bar0 + 8u * (kX + 4 + 2 * MS + SHS + s); };
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   auto meta_src = [&](int s) {
     return reinterpret_cast<int*>(smem + C::kOffMeta + s * C::kMetaBytes);
@@ -245,6 +257,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   auto meta_asc = [&](int s) { return reinterpret_cast<float*>(meta_src(s) + 2 * TN); };
   auto meta_rs = [&](int s) { return meta_src(s) + 3 * TN; };     // biased: -128 * rowsum
   auto meta_last = [&](int s) { return meta_src(s) + 4 * TN; };  // [2] per gather warp
+  auto meta_cs = [&](int s) { return reinterpret_cast<float*>(meta_src(s) + 4 * TN + 4); };
 
   if (tid == 0) {
     for (int s = 0; s < SP; ++s) {
@@ -258,10 +271,15 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(acc_full(s), C::kIssuers);
       mbar_init(acc_empty(s), 4);
-      mbar_init(meta_full(s), 2);
-      mbar_init(meta_empty(s), 4);
+    }
+    for (int s = 0; s < SHS; ++s) {
       mbar_init(sh_full(s), 1);
       mbar_init(sh_empty(s), C::kDecodeWarps);
+    }
+    for (int s = 0; s < MS; ++s) {
+      // metadata warps (two, or one in the tiled modes) + the channel-scale copy
+      mbar_init(meta_full(s), p.b_mode != 0 ? 2 : 3);
+      mbar_init(meta_empty(s), 4);
     }
     mbar_fence_init();
   }
@@ -306,8 +324,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           const int ks = ks0 + s;
           if (s % C::kShChunk == 0) {
             // smem: [2 * kShChunk shift rows][128 B] (SwiGLU: gate 64 B | up 64 B)
-            const int sl = cc & 1;
-            mbar_wait(sh_empty(sl), ((cc >> 1) & 1) ^ 1, kErrWaitPackedEmpty);
+            const int sl = cc % SHS;
+            mbar_wait(sh_empty(sl), ((cc / SHS) & 1) ^ 1, kErrWaitPackedEmpty);
             mbar_arrive_expect_tx(sh_full(sl), sh_bytes);
             const uint32_t dsts = smem_u32(smem + C::kOffSh + sl * C::kShSlotBytes);
             const int sh_row = it.expert * p.ss_per_expert + ks * 2;
@@ -343,11 +361,12 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         if (!it.valid) continue;
         int ks0, nks;
         k_range(it, ks0, nks);
-        const int ms = t & 1;
+        const int ms = t % MS;
         const int as = t % AS;
-        mbar_wait(meta_full(ms), (t >> 1) & 1, kErrWaitMeta);
+        mbar_wait(meta_full(ms), (t / MS) & 1, kErrWaitMeta);
         const uint32_t idesc = kBiased ? idesc_u8s8(128, n_mma_of(ms)) : idesc_i8(128, n_mma_of(ms));
         mbar_wait(acc_empty(as), ((t / AS) & 1) ^ 1, kErrWaitAccEmpty);
+        if (j == 0) DSV4_TRACE_EV(12, t);
         tc_fence_after();
         const uint32_t d_tmem = tmem + (as * C::kIssuers + j) * C::kAccCols;
         const int s_first = static_cast<int>((j - static_cast<int>(g % C::kIssuers) + C::kIssuers) % C::kIssuers);
@@ -377,111 +396,165 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       }
     }
   } else if (warp < 4) {
-    // ------------------- token metadata + activation gather -------------------
-    const int gt = tid - 64;
-    uint32_t g = 0, t = 0;
+    // ------------------- token metadata + activation tiles -------------------
+    // Tiled modes (b_mode 1, 2): warp 2 writes the metadata of every item and
+    // warp 3 loads the token tile of every stage (it needs only the block's
+    // first row, so it never waits for metadata).  gather4 mode (b_mode 0):
+    // both warps write the metadata, then take alternate stages, gathering
+    // the rows the metadata names.
+    const bool tiled = p.b_mode != 0;
     const uint64_t pol = l2_policy_evict_last();  // token rows are re-read by every row tile
-    if (gt == 0) tma_prefetch_desc(&p.map_act);
-    for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-      const Item it = get_item(p, i, n_blocks);
-      if (!it.valid) continue;
-      int ks0, nks;
-      k_range(it, ks0, nks);
-      const int ms = t & 1;
-      mbar_wait(meta_empty(ms), ((t >> 1) & 1) ^ 1, kErrWaitMeta);
-      int* src_s = meta_src(ms);
-      int* orow_s = meta_orow(ms);
-      float* asc_s = meta_asc(ms);
-      int* rs_s = meta_rs(ms);
-      int my_last = -1;
-      for (int jj = gt; jj < TN; jj += 64) {
-        int src = -1, orow = -1;
-        float asc = 0.f;
-        if (p.moe) {
-          if (jj < p.block_m) {
-            const int pos = it.b * p.block_m + jj;
-            const int slot = __ldg(p.sorted_ids + pos);
-            if (slot >= 0 && slot < p.num_valid) {
-              src = p.a_row_mode == 2 ? pos : (p.a_row_mode == 1 ? slot : slot / p.topk);
-              orow = p.out_sorted ? pos : slot;
+    if (tiled && warp == 3) {
+      if (lane == 0) {
+        tma_prefetch_desc(&p.map_act);
+        uint32_t g = 0;
+        for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+          const Item it = get_item(p, i, n_blocks);
+          if (!it.valid) continue;
+          int ks0, nks;
+          k_range(it, ks0, nks);
+          const int row0 = p.moe ? it.b * p.block_m : it.b * TN;
+          for (int s = 0; s < nks; ++s, ++g) {
+            const int sb = g % S;
+            mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+            DSV4_TRACE_EV(7, g);
+            const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
+            if (p.b_mode == 2) {
+              // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves
+              mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(C::kBBytes));
+              tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ab_full(sb), pol);
+            } else {
+              const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
+              mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * C::kBHalf));
+              tma_load_2d(b_base, &p.map_act, (ks0 + s) * 256, row0, ab_full(sb), pol);
+              if (nhalf == 2)
+                tma_load_2d(b_base + C::kBHalf, &p.map_act, (ks0 + s) * 256 + 128, row0,
+                            ab_full(sb), pol);
+            }
+            DSV4_TRACE_EV(4, g);
+          }
+        }
+      }
+    } else {
+      const int nthr = tiled ? 32 : 64;
+      const int gt = tid - 64;  // < nthr
+      uint32_t g = 0, t = 0;
+      if (gt == 0 && !tiled) tma_prefetch_desc(&p.map_act);
+      for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+        const Item it = get_item(p, i, n_blocks);
+        if (!it.valid) continue;
+        int ks0, nks;
+        k_range(it, ks0, nks);
+        const int ms = t % MS;
+        mbar_wait(meta_empty(ms), ((t / MS) & 1) ^ 1, kErrWaitMeta);
+        if (gt == 0) {
+          // channel scales of the item's 128 weight rows, copied into the
+          // metadata slot (a cold load in the epilogue costs microseconds)
+          if (EPI == kEpiI32) {
+            mbar_arrive(meta_full(ms));
+          } else {
+            const float* cs_e = p.cs + static_cast<int64_t>(it.expert) * p.n;
+            const uint32_t dcs = smem_u32(meta_cs(ms));
+            mbar_arrive_expect_tx(meta_full(ms), 512);
+            if (EPI == kEpiSwiglu) {
+              bulk_g2s(dcs, cs_e + it.y * 64, 256, meta_full(ms), pol);
+              bulk_g2s(dcs + 256, cs_e + p.inter + it.y * 64, 256, meta_full(ms), pol);
+            } else {
+              bulk_g2s(dcs, cs_e + it.y * 128, 512, meta_full(ms), pol);
             }
           }
-        } else {
-          const int m = it.b * TN + jj;
-          if (m < p.m) src = orow = m;
         }
-        if (src >= p.a_rows) src = -1, orow = -1;
-        if (src >= 0) {
-          asc = p.a_scale != nullptr ? __ldg(p.a_scale + src) : 0.f;
-          my_last = jj;
+        int* src_s = meta_src(ms);
+        int* orow_s = meta_orow(ms);
+        float* asc_s = meta_asc(ms);
+        int* rs_s = meta_rs(ms);
+        const bool by_pos = p.moe && p.a_row_mode == 2;
+        int my_last = -1;
+        for (int jj = gt; jj < TN; jj += nthr) {
+          int src = -1, orow = -1;
+          float asc = 0.f;
+          int rs = 0;
+          if (p.moe) {
+            if (jj < p.block_m) {
+              const int pos = it.b * p.block_m + jj;
+              // sorted rows: scale and row sum are indexed by position, so
+              // their loads need not wait for the slot id
+              float asc_pos = 0.f;
+              int rs_pos = 0;
+              if (by_pos) {
+                asc_pos = __ldg(p.a_scale + pos);
+                if (kBiased) rs_pos = __ldg(p.a_rowsum + pos);
+              }
+              const int slot = __ldg(p.sorted_ids + pos);
+              if (slot >= 0 && slot < p.num_valid) {
+                src = by_pos ? pos : (p.a_row_mode == 1 ? slot : slot / p.topk);
+                orow = p.out_sorted ? pos : slot;
+                asc = asc_pos;
+                rs = rs_pos;
+              }
+            }
+          } else {
+            const int m = it.b * TN + jj;
+            if (m < p.m) src = orow = m;
+          }
+          if (src >= p.a_rows) src = -1, orow = -1;
+          if (src >= 0) {
+            if (!by_pos) {
+              asc = p.a_scale != nullptr ? __ldg(p.a_scale + src) : 0.f;
+              if (kBiased) rs = __ldg(p.a_rowsum + src);
+            }
+            my_last = jj;
+          }
+          src_s[jj] = src;
+          orow_s[jj] = orow;
+          asc_s[jj] = asc;
+          if (kBiased) rs_s[jj] = src >= 0 ? -128 * rs : 0;
         }
-        src_s[jj] = src;
-        orow_s[jj] = orow;
-        asc_s[jj] = asc;
-        if (kBiased) rs_s[jj] = src >= 0 ? -128 * __ldg(p.a_rowsum + src) : 0;
-      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-        my_last = max(my_last, __shfl_xor_sync(0xffffffffu, my_last, o));
-      if (lane == 0) meta_last(ms)[warp - 2] = my_last;
-      named_bar_sync(2, 64);
-      const int n_mma = n_mma_of(ms);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(meta_full(ms));
-      {
-        // Warps 2 and 3 take alternate stages.  gather4 (b_mode 0) fetches only
-        // the rows up to the last valid one (4 at a time, lane l -> rows
-        // 4l .. 4l+3 of both 128-K halves); the tiled modes load the block's TN
-        // rows from row0 (rows past the tensor read as zeros).  The MMA columns
-        // beyond the last valid row are never stored.
-        const int last = max(meta_last(ms)[0], meta_last(ms)[1]);
-        const int n_rows = ((max(last, 0) + 4) / 4) * 4;
-        const int row0 = p.moe ? it.b * p.block_m : it.b * TN;
-        for (int s = 0; s < nks; ++s, ++g) {
-          if (static_cast<int>(g & 1) != warp - 2) continue;
-          const int sb = g % S;
-          const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
-          if (p.b_mode != 0) {
+        for (int o = 16; o > 0; o >>= 1)
+          my_last = max(my_last, __shfl_xor_sync(0xffffffffu, my_last, o));
+        if (lane == 0) {
+          meta_last(ms)[warp - 2] = my_last;
+          if (tiled) meta_last(ms)[1] = -1;
+        }
+        if (tiled)
+          __syncwarp();
+        else
+          named_bar_sync(2, 64);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(meta_full(ms));
+        if (!tiled) {
+          // Warps 2 and 3 take alternate stages and gather only the rows up to
+          // the last valid one (4 at a time, lane l -> rows 4l .. 4l+3 of both
+          // 128-K halves); the MMA columns beyond are never stored.
+          const int last = max(meta_last(ms)[0], meta_last(ms)[1]);
+          const int n_rows = ((max(last, 0) + 4) / 4) * 4;
+          for (int s = 0; s < nks; ++s, ++g) {
+            if (static_cast<int>(g & 1) != warp - 2) continue;
+            const int sb = g % S;
+            const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
             if (lane == 0) {
               mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
               DSV4_TRACE_EV(7, g);
-              const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
-              if (p.b_mode == 2) {
-                // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves
-                mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(C::kBBytes));
-                tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ab_full(sb), pol);
-              } else {
-                mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * C::kBHalf));
-                tma_load_2d(b_base, &p.map_act, (ks0 + s) * 256, row0, ab_full(sb), pol);
-                if (nhalf == 2)
-                  tma_load_2d(b_base + C::kBHalf, &p.map_act, (ks0 + s) * 256 + 128, row0,
-                              ab_full(sb), pol);
-              }
-              DSV4_TRACE_EV(4, g);
+              mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * n_rows * 128));
             }
-            continue;
+            __syncwarp();
+            const int x0 = (ks0 + s) * 256;
+            const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
+            for (int r = lane * 4; r < n_rows; r += 128) {
+              const uint32_t dst = b_base + (r >> 3) * 1024 + (r & 7) * 128;
+              // padding rows read the out-of-range row -1: zeros
+              tma_gather4(dst, &p.map_act, x0, src_s[r], src_s[r + 1], src_s[r + 2],
+                          src_s[r + 3], ab_full(sb), pol);
+              if (nhalf == 2)
+                tma_gather4(dst + C::kBHalf, &p.map_act, x0 + 128, src_s[r], src_s[r + 1],
+                            src_s[r + 2], src_s[r + 3], ab_full(sb), pol);
+            }
+            if (lane == 0) DSV4_TRACE_EV(4, g);
           }
-          if (lane == 0) {
-            mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
-            DSV4_TRACE_EV(7, g);
-            mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * n_rows * 128));
-          }
-          __syncwarp();
-          const int x0 = (ks0 + s) * 256;
-          const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
-          for (int r = lane * 4; r < n_rows; r += 128) {
-            const uint32_t dst = b_base + (r >> 3) * 1024 + (r & 7) * 128;
-            // padding rows read the out-of-range row -1: zeros
-            tma_gather4(dst, &p.map_act, x0, src_s[r], src_s[r + 1], src_s[r + 2], src_s[r + 3],
-                        ab_full(sb), pol);
-            if (nhalf == 2)
-              tma_gather4(dst + C::kBHalf, &p.map_act, x0 + 128, src_s[r], src_s[r + 1],
-                          src_s[r + 2], src_s[r + 3], ab_full(sb), pol);
-          }
-          if (lane == 0) DSV4_TRACE_EV(4, g);
         }
+        ++t;
       }
-      ++t;
     }
   } else if (warp < 8) {
     // -------------------------------- epilogue --------------------------------
@@ -496,10 +569,11 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       if (!it.valid) continue;
       int ks0, nks;
       k_range(it, ks0, nks);
-      const int ms = t & 1;
+      const int ms = t % MS;
       const int as = t % AS;
-      mbar_wait(meta_full(ms), (t >> 1) & 1, kErrWaitMeta);
+      mbar_wait(meta_full(ms), (t / MS) & 1, kErrWaitMeta);
       mbar_wait(acc_full(as), (t / AS) & 1, kErrWaitAccFull);
+      if (tid == 128) DSV4_TRACE_EV(10, t);
       tc_fence_after();
       const int* orow_s = meta_orow(ms);
       const float* asc_s = meta_asc(ms);
@@ -509,7 +583,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       uint32_t accmask = 0;
       for (int q = 0; q < min(nks, C::kIssuers); ++q) accmask |= 1u << ((g + q) % C::kIssuers);
       const uint32_t t0 = tmem + (as * C::kIssuers) * C::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-      const float* cs_e = p.cs + static_cast<int64_t>(it.expert) * p.n;
+      const float csn = EPI == kEpiI32 ? 0.f : meta_cs(ms)[row_local];
       auto load16 = [&](int c0, int32_t (&v)[16]) {
 #pragma unroll
         for (int q = 0; q < 16; ++q) v[q] = kBiased ? rs_s[c0 + q] : 0;
@@ -524,10 +598,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       };
 
       if (EPI == kEpiSwiglu) {
-        const bool is_up = row_local >= 64;
-        const int i_local = row_local & 63;
         const int j0 = it.y * 64;
-        const float csn = __ldg(cs_e + (is_up ? p.inter : 0) + j0 + i_local);
         for (int c0 = 0; c0 < n_mma; c0 += 16) {
           int32_t v[16];
           load16(c0, v);
@@ -560,7 +631,6 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         }
       } else {
         const int n_g = it.y * 128 + row_local;
-        const float csn = (EPI == kEpiBf16) ? __ldg(cs_e + n_g) : 0.f;
         for (int c0 = 0; c0 < n_mma; c0 += 16) {
           int32_t v[16];
           load16(c0, v);
@@ -580,6 +650,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       }
       tc_fence_before();
       __syncwarp();
+      if (tid == 128) DSV4_TRACE_EV(11, t);
       if (lane == 0) {
         mbar_arrive(acc_empty(as));
         mbar_arrive(meta_empty(ms));
@@ -610,8 +681,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       int s = static_cast<int>((grp - static_cast<int>(g % C::kDecodeGroups) + C::kDecodeGroups) %
                                C::kDecodeGroups);
       for (int c0 = 0; c0 < nks; c0 += C::kShChunk, ++cc) {
-        mbar_wait(sh_full(cc & 1), (cc >> 1) & 1, kErrWaitPackedFull);
-        const uint8_t* SHC = smem + C::kOffSh + (cc & 1) * C::kShSlotBytes;
+        mbar_wait(sh_full(cc % SHS), (cc / SHS) & 1, kErrWaitPackedFull);
+        const uint8_t* SHC = smem + C::kOffSh + (cc % SHS) * C::kShSlotBytes;
         const int c1 = min(nks, c0 + C::kShChunk);
         for (; s < c1; s += C::kDecodeGroups) {
           const uint32_t gs = g + static_cast<uint32_t>(s);
@@ -679,7 +750,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           if (lane == 0 && quarter == 0) DSV4_TRACE_EV(5, gs);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(sh_empty(cc & 1));
+        if (lane == 0) mbar_arrive(sh_empty(cc % SHS));
       }
       g += nks;
     }
