@@ -142,7 +142,8 @@ class Layer:
         import torch
         import dsv4_b200 as D
         self.D, self.w, self.m, self.dev = D, weights, m, dev
-        self.bm, self.bn = D.select_mxfp4_int8_moe_tile_shape(m, TOPK, E)
+        _, self.bn = D.select_mxfp4_int8_moe_tile_shape(m, TOPK, E)
+        self.bm = D.select_sorted_block_m(m, TOPK, E)
         self.routed = torch.empty((m * TOPK, H), device=dev, dtype=torch.bfloat16)
         self.out = torch.empty((m, H), device=dev, dtype=torch.bfloat16)
         self.ev = []
@@ -173,7 +174,7 @@ class Layer:
             evs[3].record()
             self.ev.append(evs)
         J.mxfp4_int8_moe_reduce(self.routed, tw, self.out, hidden_size=H, intermediate_size=I,
-                                topk=TOPK, block_m=self.bm, num_valid_tokens=m * TOPK)
+                                topk=TOPK, block_m=min(self.bm, 128), num_valid_tokens=m * TOPK)
         return self.out
 
     def gemm_ms(self):

@@ -117,9 +117,9 @@ struct TcGemmParams {
 // see a stale phase as complete).  Every role therefore takes stage g by
 // g mod (its count), and each ring depth is a multiple of those counts, so
 // each slot always has the same waiter:
-//   decode group  g % kDecodeGroups   -> kDecodeGroups | kStages, kStagesP
-//   MMA issuer    g % kIssuers        -> kIssuers | kStages
-//   gather warp   g % 2               -> 2 | kStages
+//   decode group  g % kDecodeGroups   -> kDecodeGroups | kStagesA, kStagesP
+//   MMA issuer    g % kIssuers        -> kIssuers | kStagesA, kStagesB
+//   gather warp   g % 2               -> 2 | kStagesB
 template <int TN>
 struct TcGemmCfg {
   static constexpr int kBHalf = TN * 128;        // one 128-K SW128 sub-tile of B
@@ -134,33 +134,38 @@ struct TcGemmCfg {
   // MMA issuer threads, one accumulator each: an issuer sharing its SM
   // sub-partition with three decode warps issues a 16-token MMA in ~200
   // cycles, so 16-token tiles (8 MMAs per stage) need three
-  static constexpr int kIssuers = TN <= 16 ? 3 : 2;
+  // (256-token tiles: an N=256 MMA takes 128 tensor cycles, more than its
+  // issue cost, so one issuer keeps the tensor pipe busy)
+  static constexpr int kIssuers = TN <= 16 ? 3 : (TN <= 128 ? 2 : 1);
   static constexpr int kDecodeGroups = TN <= 64 ? 3 : 4;  // groups of 4 decode warps
-  static constexpr int kStages = TN <= 64 ? 6 : 4;        // A (TMEM, 64 cols) + B (smem) ring
+  // A ring (decoded weights in TMEM, 64 columns = 256 K per slot) and B ring
+  // (token tiles in shared memory) have their own depths and barriers
+  static constexpr int kStagesA = TN <= 64 ? 6 : 4;
+  static constexpr int kStagesB = TN <= 64 ? 6 : (TN <= 128 ? 4 : 2);
   // accumulator sets per issuer: two where TMEM has room, so the MMAs of the
   // next item do not wait for the epilogue of this one
-  static constexpr int kAccSlots = kIssuers * 2 * kAccCols + kStages * 64 <= 512 ? 2 : 1;
+  static constexpr int kAccSlots = kIssuers * 2 * kAccCols + kStagesA * 64 <= 512 ? 2 : 1;
   // TMEM (512 columns): [issuer accumulators], then 64-column A slots
   static constexpr int kAColBase = kIssuers * kAccSlots * kAccCols;
   static constexpr int kTmemCols = 512;
   static constexpr int kStgBytes = 16 * 128 * 2;   // SwiGLU staging (16 cols x 128 rows bf16)
   // src, orow, ascale, rowsum [TN]; per-warp last [4]; channel scales [128]
   static constexpr int kMetaBytes = TN * 16 + 16 + 512;
-  static constexpr int kMetaSlots = 4;  // items of metadata prepared ahead
-  static constexpr int kFixed = kStages * kBBytes + kShSlots * kShSlotBytes + kStgBytes + kMetaSlots * kMetaBytes + 1024;
+  static constexpr int kMetaSlots = TN <= 128 ? 4 : 2;  // items of metadata prepared ahead
+  static constexpr int kFixed = kStagesB * kBBytes + kShSlots * kShSlotBytes + kStgBytes + kMetaSlots * kMetaBytes + 1024;
   static constexpr int kBudget = 227 * 1024 - 1024;  // minus alignment slack
   static constexpr int kStagesPRaw = (kBudget - kFixed) / kPBytes;
   static constexpr int kStagesPCap = kStagesPRaw > 16 ? 16 : kStagesPRaw;
   static constexpr int kStagesP = kStagesPCap / kDecodeGroups * kDecodeGroups;
   static constexpr int kOffB = 0;
-  static constexpr int kOffP = kOffB + kStages * kBBytes;
+  static constexpr int kOffP = kOffB + kStagesB * kBBytes;
   static constexpr int kOffSh = kOffP + kStagesP * kPBytes;
   static constexpr int kOffStg = kOffSh + kShSlots * kShSlotBytes;
   static constexpr int kOffMeta = kOffStg + kStgBytes;
   static constexpr int kOffBar = kOffMeta + kMetaSlots * kMetaBytes;
-  // barriers: pk_full/empty[SP], ab_full/empty[S], acc_full/empty[2],
+  // barriers: pk_full/empty[SP], a_full/empty[SA], b_full/empty[SB], acc_full/empty[2],
   // meta_full/empty[kMetaSlots], sh_full/empty[kShSlots]
-  static constexpr int kNumBars = 2 * kStagesP + 2 * kStages + 4 + 2 * kMetaSlots + 2 * kShSlots;
+  static constexpr int kNumBars = 2 * kStagesP + 2 * kStagesA + 2 * kStagesB + 4 + 2 * kMetaSlots + 2 * kShSlots;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
@@ -169,11 +174,12 @@ struct TcGemmCfg {
   static constexpr int kIssuer1Warp = 8 + kDecodeWarps;
   static constexpr int kWarps = kIssuer1Warp + kIssuers - 1;
   static constexpr int kThreads = kWarps * 32;
-  static_assert(TN % 16 == 0 && TN >= 16 && TN <= 128, "token tile");
-  static_assert(kStages % kDecodeGroups == 0 && kStages % kIssuers == 0 && kStages % 2 == 0,
+  static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "token tile");
+  static_assert(kStagesA % kDecodeGroups == 0 && kStagesA % kIssuers == 0 &&
+                    kStagesB % kIssuers == 0 && kStagesB % 2 == 0,
                 "ring discipline");
   static_assert(kStagesP % kDecodeGroups == 0 && kStagesP >= 3, "packed ring");
-  static_assert(kAColBase + kStages * 64 <= kTmemCols, "TMEM budget");
+  static_assert(kAColBase + kStagesA * 64 <= kTmemCols, "TMEM budget");
   static_assert(kSmemLaunch <= 227 * 1024, "shared memory budget");
   static_assert(kBHalf % 1024 == 0 && kOffMeta % 16 == 0 && kOffBar % 8 == 0, "alignment");
 };
@@ -213,7 +219,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   constexpr int EPI = EPIF & 3;
   constexpr bool kBiased = (EPIF & kEpiBiased) != 0;
   using C = TcGemmCfg<TN>;
-  constexpr int S = C::kStages;
+  constexpr int SA = C::kStagesA;
+  constexpr int SB = C::kStagesB;
   constexpr int SP = C::kStagesP;
   constexpr int AS = C::kAccSlots;
 
@@ -238,9 +245,11 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   const uint32_t bar0 = smem_u32(smem + C::kOffBar);
   auto pk_full = [&](int s) { return bar0 + 8u * s; };
   auto pk_empty = [&](int s) { return bar0 + 8u * (SP + s); };
-  auto ab_full = [&](int s) { return bar0 + 8u * (2 * SP + s); };
-  auto ab_empty = [&](int s) { return bar0 + 8u * (2 * SP + S + s); };
-  constexpr int kX = 2 * SP + 2 * S;
+  auto a_full = [&](int s) { return bar0 + 8u * (2 * SP + s); };
+  auto a_empty = [&](int s) { return bar0 + 8u * (2 * SP + SA + s); };
+  auto b_full = [&](int s) { return bar0 + 8u * (2 * SP + 2 * SA + s); };
+  auto b_empty = [&](int s) { return bar0 + 8u * (2 * SP + 2 * SA + SB + s); };
+  constexpr int kX = 2 * SP + 2 * SA + 2 * SB;
   auto acc_full = [&](int s) { return bar0 + 8u * (kX + s); };
   auto acc_empty = [&](int s) { return bar0 + 8u * (kX + 2 + s); };
   constexpr int MS = C::kMetaSlots;
@@ -264,9 +273,13 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       mbar_init(pk_full(s), 1);
       mbar_init(pk_empty(s), 4);
     }
-    for (int s = 0; s < S; ++s) {
-      mbar_init(ab_full(s), 4 + 1);  // one decode group (4 warps) + one gather lane
-      mbar_init(ab_empty(s), 1);
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(a_full(s), 4);  // one decode group (4 warps)
+      mbar_init(a_empty(s), 1);
+    }
+    for (int s = 0; s < SB; ++s) {
+      mbar_init(b_full(s), 1);  // the loading lane (+ transaction bytes)
+      mbar_init(b_empty(s), 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(acc_full(s), C::kIssuers);
@@ -372,13 +385,15 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         const int s_first = static_cast<int>((j - static_cast<int>(g % C::kIssuers) + C::kIssuers) % C::kIssuers);
         for (int s = s_first; s < nks; s += C::kIssuers) {
           const uint32_t gs = g + s;
-          const int sa = gs % S;
+          const int sa = gs % SA;
+          const int sb = gs % SB;
           DSV4_TRACE_EV(9, gs);
-          mbar_wait(ab_full(sa), (gs / S) & 1, kErrWaitAbFull);
+          mbar_wait(b_full(sb), (gs / SB) & 1, kErrWaitAbFull);
+          mbar_wait(a_full(sa), (gs / SA) & 1, kErrWaitAbFull);
           DSV4_TRACE_EV(3, gs);
           tc_fence_after();
           const uint32_t a_tmem = tmem + C::kAColBase + sa * 64;
-          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((sa * C::kBBytes) >> 4);
+          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((sb * C::kBBytes) >> 4);
           const int nkb = stage_kb(ks0 + s);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -387,7 +402,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
                         bdesc + static_cast<uint64_t>(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4),
                         idesc, (s > s_first || kk > 0) ? 1u : 0u);
           }
-          mma_commit(ab_empty(sa));
+          mma_commit(a_empty(sa));
+          mma_commit(b_empty(sb));
           DSV4_TRACE_EV(6, gs);
         }
         mma_commit(acc_full(as));
@@ -415,21 +431,21 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           k_range(it, ks0, nks);
           const int row0 = p.moe ? it.b * p.block_m : it.b * TN;
           for (int s = 0; s < nks; ++s, ++g) {
-            const int sb = g % S;
-            mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+            const int sb = g % SB;
+            mbar_wait(b_empty(sb), ((g / SB) & 1) ^ 1, kErrWaitAbEmpty);
             DSV4_TRACE_EV(7, g);
             const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
             if (p.b_mode == 2) {
               // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves
-              mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(C::kBBytes));
-              tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ab_full(sb), pol);
+              mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(C::kBBytes));
+              tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, b_full(sb), pol);
             } else {
               const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
-              mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * C::kBHalf));
-              tma_load_2d(b_base, &p.map_act, (ks0 + s) * 256, row0, ab_full(sb), pol);
+              mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(nhalf * C::kBHalf));
+              tma_load_2d(b_base, &p.map_act, (ks0 + s) * 256, row0, b_full(sb), pol);
               if (nhalf == 2)
                 tma_load_2d(b_base + C::kBHalf, &p.map_act, (ks0 + s) * 256 + 128, row0,
-                            ab_full(sb), pol);
+                            b_full(sb), pol);
             }
             DSV4_TRACE_EV(4, g);
           }
@@ -531,12 +547,12 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           const int n_rows = ((max(last, 0) + 4) / 4) * 4;
           for (int s = 0; s < nks; ++s, ++g) {
             if (static_cast<int>(g & 1) != warp - 2) continue;
-            const int sb = g % S;
+            const int sb = g % SB;
             const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
             if (lane == 0) {
-              mbar_wait(ab_empty(sb), ((g / S) & 1) ^ 1, kErrWaitAbEmpty);
+              mbar_wait(b_empty(sb), ((g / SB) & 1) ^ 1, kErrWaitAbEmpty);
               DSV4_TRACE_EV(7, g);
-              mbar_arrive_expect_tx(ab_full(sb), static_cast<uint32_t>(nhalf * n_rows * 128));
+              mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(nhalf * n_rows * 128));
             }
             __syncwarp();
             const int x0 = (ks0 + s) * 256;
@@ -545,10 +561,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
               const uint32_t dst = b_base + (r >> 3) * 1024 + (r & 7) * 128;
               // padding rows read the out-of-range row -1: zeros
               tma_gather4(dst, &p.map_act, x0, src_s[r], src_s[r + 1], src_s[r + 2],
-                          src_s[r + 3], ab_full(sb), pol);
+                          src_s[r + 3], b_full(sb), pol);
               if (nhalf == 2)
                 tma_gather4(dst + C::kBHalf, &p.map_act, x0 + 128, src_s[r], src_s[r + 1],
-                            src_s[r + 2], src_s[r + 3], ab_full(sb), pol);
+                            src_s[r + 2], src_s[r + 3], b_full(sb), pol);
             }
             if (lane == 0) DSV4_TRACE_EV(4, g);
           }
@@ -621,7 +637,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
                 gv = fminf(gv, lim);
                 up = fminf(fmaxf(up, -lim), lim);
               }
-              const float sg = __bfloat162float(f2bf(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)))));
+              // silu in fast fp32 (MUFU exp2 / reciprocal): the result is
+              // rounded to bf16, where it differs from the IEEE-exact form by
+              // at most one ulp, and rarely
+              const float sg = __bfloat162float(f2bf(__fdividef(gv, 1.0f + __expf(-gv))));
               h[u] = f2bf(__fmul_rn(sg, up));
             }
             *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo + j0 + i0) =
@@ -687,7 +706,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         for (; s < c1; s += C::kDecodeGroups) {
           const uint32_t gs = g + static_cast<uint32_t>(s);
           const int sp = gs % SP;
-          const int sa = gs % S;
+          const int sa = gs % SA;
           const int nkb = stage_kb(ks0 + s);
           if (lane == 0 && quarter == 0) DSV4_TRACE_EV(8, gs);
           mbar_wait(pk_full(sp), (gs / SP) & 1, kErrWaitPackedFull);
@@ -711,7 +730,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           // semantics, ordering the loads above).
           __syncwarp();
           if (lane == 0) mbar_arrive(pk_empty(sp));
-          mbar_wait(ab_empty(sa), ((gs / S) & 1) ^ 1, kErrWaitAbEmpty);
+          mbar_wait(a_empty(sa), ((gs / SA) & 1) ^ 1, kErrWaitAbEmpty);
           if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, gs);
           tc_fence_after();
           const uint32_t tcol = tmem + t_lane + C::kAColBase + sa * 64;
@@ -746,7 +765,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(ab_full(sa));
+          if (lane == 0) mbar_arrive(a_full(sa));
           if (lane == 0 && quarter == 0) DSV4_TRACE_EV(5, gs);
         }
         __syncwarp();

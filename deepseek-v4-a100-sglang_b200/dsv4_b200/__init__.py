@@ -16,6 +16,7 @@ from .mxfp4_int8_moe import (  # noqa: F401
     quantize_per_token_int8,
     remap_mxfp4_weight_for_int8,
     select_mxfp4_int8_moe_tile_shape,
+    select_sorted_block_m,
 )
 from .jit_ops import (  # noqa: F401
     mxfp4_int8_dense_gemm,
@@ -23,6 +24,10 @@ from .jit_ops import (  # noqa: F401
     mxfp4_int8_moe_gemm,
     mxfp4_int8_moe_gemm_swiglu,
     mxfp4_int8_moe_reduce,
+    moe_sort_rows,
+    quantize_sorted_int8,
+    mxfp4_int8_moe_gemm_sorted,
+    mxfp4_int8_moe_gemm_swiglu_sorted,
     prewarm_mxfp4_int8_dense_jit_module,
     prewarm_mxfp4_int8_moe_jit_modules,
 )

@@ -159,6 +159,11 @@ def mxfp4_int8_moe_gemm_swiglu(a_q, a_scale, b_mxfp4, b_shift2, b_channel_scale,
 
 # ---- expert-sorted row pipeline (B200 fast path; same arithmetic) ----
 
+def _sorted_bm(block_m: int) -> int:
+    """The sorted-row GEMMs also take 256-token tiles; validate the rest as usual."""
+    return 128 if block_m == 256 else block_m
+
+
 def moe_sort_rows(a_q, a_scale, sorted_token_ids, num_tokens_post_padded, *, topk: int,
                   num_valid_tokens: int, source_rows_are_slots: bool = False):
     """Copy the routed INT8 rows into the order of the aligned permutation:
@@ -210,7 +215,7 @@ def mxfp4_int8_moe_gemm_swiglu_sorted(a_sorted, a_scale, a_rowsum, b_mxfp4, b_sh
                                       clamp_limit: float | None = None) -> None:
     """:func:`mxfp4_int8_moe_gemm_swiglu` on sorted rows: ``out``
     ``[sorted_capacity, I]`` bf16 by sorted position."""
-    _validate_template_args(hidden_size, intermediate_size, topk, block_m, 128)
+    _validate_template_args(hidden_size, intermediate_size, topk, _sorted_bm(block_m), 128)
     n, k = 2 * intermediate_size, hidden_size
     cap = sorted_token_ids.numel()
     e = _moe_common_checks(a_sorted.view(cap, k), a_scale, b_mxfp4, b_shift2, b_channel_scale,
@@ -233,7 +238,7 @@ def mxfp4_int8_moe_gemm_sorted(a_sorted, a_scale, a_rowsum, b_mxfp4, b_shift2, b
                                num_valid_tokens: int) -> None:
     """W2 of :func:`mxfp4_int8_moe_gemm` (``source_rows_are_slots``) on
     sorted rows: ``routed_out`` ``[num_valid, H]`` by routed slot."""
-    _validate_template_args(hidden_size, intermediate_size, topk, block_m, 128)
+    _validate_template_args(hidden_size, intermediate_size, topk, _sorted_bm(block_m), 128)
     n, k = hidden_size, intermediate_size
     cap = sorted_token_ids.numel()
     e = _moe_common_checks(a_sorted.view(cap, k), a_scale, b_mxfp4, b_shift2, b_channel_scale,

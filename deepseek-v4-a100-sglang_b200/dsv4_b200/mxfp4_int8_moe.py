@@ -226,6 +226,19 @@ def select_mxfp4_int8_moe_tile_shape(m: int, topk: int, experts: int) -> tuple[i
     return _select_moe_tile_shape(m, topk, experts)
 
 
+def select_sorted_block_m(m: int, topk: int, experts: int) -> int:
+    """Token tile of the expert-sorted fast path: the tile policy above,
+    widened to 256 tokens (N=256 MMAs: one weight decode and one MMA
+    instruction per 256 tokens) when the average routed tokens per expert
+    reach 256 and no tile is forced through the environment."""
+    block_m, _ = _select_moe_tile_shape(m, topk, experts)
+    forced = os.environ.get("SGLANG_DSV4_MXFP4_INT8_BLOCK_M", "").strip()
+    avg = (m * topk + max(experts, 1) - 1) // max(experts, 1)
+    if block_m == _MAX_BLOCK_M and not forced and avg >= 256:
+        return 256
+    return block_m
+
+
 def align_capacity(numel: int, num_experts: int, block_size: int) -> int:
     """PYMOE:848-851."""
     if numel < num_experts + 1:
@@ -283,7 +296,8 @@ def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWei
     m = hidden_states.shape[0]
     topk = topk_ids_i32.shape[1]
     experts = weights.w13_mxfp4.shape[0]
-    block_m, block_n = _select_moe_tile_shape(m, topk, experts)
+    _, block_n = _select_moe_tile_shape(m, topk, experts)
+    block_m = select_sorted_block_m(m, topk, experts)
     sorted_ids, expert_ids, ntpp = moe_align_block_size(topk_ids_i32, block_m, experts)
     a13_q, a13_scale = quantize_per_token_int8(hidden_states, 0.0)
     return _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids,
@@ -326,7 +340,8 @@ def _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_
                float(routed_scaling_factor) if apply else 1.0, N.stream_of(out))
     else:
         mxfp4_int8_moe_reduce(routed_out, topk_weights_f32, out, hidden_size=hidden_size,
-                              intermediate_size=intermediate_size, topk=topk, block_m=block_m,
+                              intermediate_size=intermediate_size, topk=topk,
+                              block_m=min(block_m, _MAX_BLOCK_M),  # validated only
                               block_n=block_n, num_valid_tokens=m * topk,
                               routed_scaling_factor=routed_scaling_factor)
     return out
@@ -349,7 +364,8 @@ def mxfp4_int8_moe_forward_quantized(a_q: torch.Tensor, a_scale: torch.Tensor,
     experts = weights.w13_mxfp4.shape[0]
     if m == 0:
         return torch.empty((0, hidden_size), device=a_q.device, dtype=torch.bfloat16)
-    block_m, block_n = _select_moe_tile_shape(m, topk, experts)
+    _, block_n = _select_moe_tile_shape(m, topk, experts)
+    block_m = select_sorted_block_m(m, topk, experts)
     sorted_ids, expert_ids, ntpp = moe_align_block_size(ids, block_m, experts)
     return _moe_core(a_q.contiguous(), a_scale.contiguous(), weights, ids, w, sorted_ids,
                      expert_ids, ntpp, block_m=block_m, block_n=block_n, hidden_size=hidden_size,

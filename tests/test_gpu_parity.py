@@ -177,7 +177,12 @@ def _cm_rows(t, cap, k):  # K-chunk-major [k/128][cap][128] -> [cap][k]
     return t.view(k // 128, cap, 128).permute(1, 0, 2).reshape(cap, k).cpu().numpy()
 
 
-@pytest.mark.parametrize("case", MOE_CASES)
+# the sorted path also runs 256-token tiles (N=256 MMAs, one issuer)
+SORTED_CASES = MOE_CASES + [(8, 1200, 256, 256, 2, 256), (4, 640, 1024, 256, 4, 256),
+                            (16, 300, 512, 128, 8, 256)]
+
+
+@pytest.mark.parametrize("case", SORTED_CASES)
 def test_moe_sorted_pipeline_bit_exact(case):
     """The expert-sorted fast path (sort rows -> W13+SwiGLU -> sorted requant
     -> W2, biased-unsigned decode with row-sum correction) against the same
