@@ -470,9 +470,9 @@ def main():
                    "experts_touched": dec["touched"]},
         "roofline": {"bound": "hbm", "kernel": "W13 grouped GEMM + fused SwiGLU",
                      "achieved": w13_gbs, "peak": hbm, "unit": "GB/s", "frac": w13_gbs / hbm,
-                     # DRAM bytes per launch: the 32-expert ncu capture read+wrote 1.005x its
+                     # DRAM bytes per launch: the 32-expert ncu capture read+wrote 1.015x its
                      # algorithmic bytes (profiles/moe_decode_w13_gemm_ncu.md); scaled to this launch
-                     "traffic": dec["w13_bytes"] * 1.005, "peak_source": peak_src,
+                     "traffic": dec["w13_bytes"] * 1.015, "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": dec["w13_bytes"],
                      "launch_ms": dec["w13_ms"]},
         "layer_roofline": {"bound": "hbm", "bytes_per_step": dec["layer_bytes"],
