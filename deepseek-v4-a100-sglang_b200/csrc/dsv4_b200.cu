@@ -269,6 +269,7 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
                "null pointer argument");
   if (int r = check_weights(experts, n_rows, k, shift_stride)) return r;
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(cs) & 15) == 0, "b_channel_scale must be 16-byte aligned");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(dst) & 15) == 0, "output must be 16-byte aligned");
   DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
   DSV4_REQUIRE(block_m == 16 || block_m == 32 || block_m == 64 || block_m == 128 ||
                    (sorted_rows && block_m == 256),
@@ -351,6 +352,8 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   if (int r = check_weights(1, n, k, shift_stride)) return r;
   DSV4_REQUIRE(cs == nullptr || (reinterpret_cast<uintptr_t>(cs) & 15) == 0,
                "weight_channel_scale must be 16-byte aligned");
+  DSV4_REQUIRE(out == nullptr || (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+               "out must be 16-byte aligned");
   TcGemmParams p{};
   p.dec_m1 = 0xFFFFFFFFu;
   p.dec_hi16 = 65536u;

@@ -653,14 +653,31 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         for (int c0 = 0; c0 < n_mma; c0 += 16) {
           int32_t v[16];
           load16(c0, v);
+          if (EPI == kEpiBf16) {
+            // staged through shared memory ([token][128 channels] bf16) so a
+            // thread stores 32 contiguous bytes of one token row instead of
+            // 16 scattered 2-byte values
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const int orow = orow_s[c0 + q];
-            if (orow < 0) continue;
-            if (EPI == kEpiBf16) {
-              const float x = __fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn);
-              p.out[static_cast<int64_t>(orow) * p.ldo + n_g] = f2bf(x);
-            } else {
+            for (int q = 0; q < 16; ++q)
+              stg[q * 128 + row_local] =
+                  f2bf(__fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn));
+            named_bar_sync(1, 128);
+            const int col = e >> 3;         // token of the chunk
+            const int ch0 = (e & 7) * 16;   // 16 channels
+            const int orow = orow_s[c0 + col];
+            if (orow >= 0) {
+              const uint4* src = reinterpret_cast<const uint4*>(stg + col * 128 + ch0);
+              uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo +
+                                                    it.y * 128 + ch0);
+              dst[0] = src[0];
+              dst[1] = src[1];
+            }
+            named_bar_sync(1, 128);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const int orow = orow_s[c0 + q];
+              if (orow < 0) continue;
               p.out_i32[static_cast<int64_t>(it.z) * p.split_stride +
                         static_cast<int64_t>(orow) * p.ldo + n_g] = v[q];
             }
