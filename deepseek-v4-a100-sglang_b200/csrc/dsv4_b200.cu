@@ -216,7 +216,7 @@ int shift_chunk_rows(int stages_per_item) {
 //   b_mode 2: int8 K-chunk-major [k/128][rows][128] as 3-D {128, rows, k/128},
 //             box {128, tn, 2} (both 128-K halves of a stage in one copy)
 int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, int b_mode, int tn) {
-  DSV4_REQUIRE(tn <= 128 || b_mode != 0, "256-token tiles need tiled token rows");
+  DSV4_REQUIRE(tn <= 128 || b_mode == 2, "256-token tiles need K-chunk-major token rows");
   if (tensor_map_encoder() == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, "a_q must be 16-byte aligned");
   DSV4_REQUIRE(rows >= 1 && rows < (1ll << 31), "bad activation row count");
@@ -225,7 +225,9 @@ int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, in
     DSV4_REQUIRE(k % 128 == 0, "K-chunk-major rows need K %% 128 == 0");
     cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(k / 128)};
     cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(rows) * 128};
-    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(tn), 2};
+    // (box depth 2 / kBSplit: both 128-K halves of a stage per copy)
+    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(tn),
+                         static_cast<cuuint32_t>(2 / TcGemmCfg<256>::kBSplit)};
     r = encode_u8(&p.map_act, 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   } else {

@@ -7,7 +7,7 @@
 //
 // Orientation ("swap-AB"): the decoded weight tile is the MMA A operand
 // (M = 128 weight rows = output channels) and lives in tensor memory; the
-// gathered token rows are the B operand (N = 16..128 tokens, SW128 K-major
+// token rows are the B operand (N = 16..256 tokens, SW128 K-major
 // in shared memory); int32 accumulators in TMEM, [channel lane][token col].
 // One weight tile, once decoded, serves every token of the tile.
 //
@@ -16,11 +16,12 @@
 // same sequence, so the weight stream never drains between items.
 //
 // Issue cost shapes the design: in the issuing thread one tcgen05.mma costs
-// ~64 cycles, one mbarrier wait ~245 cycles (even when already complete) and
-// one commit ~50.  So each 128-K stage has ONE ready barrier (decoded A and
-// gathered B together) and ONE commit, and two issuer warps take alternate
-// stages of an item into two accumulators (int32 sums are exact; the
-// epilogue adds them), which halves the per-stage issue time per SM.
+// ~70 cycles alone and ~100-200 beside ALU-bound decode warps, a completed
+// mbarrier try_wait ~245 (so waits probe with test_wait first), one commit
+// ~50.  So small token tiles spread the MMAs of alternate stages over 2-3
+// issuer threads with their own accumulators (int32 sums are exact; the
+// epilogue adds them), while 256-token tiles (N=256: 128 tensor cycles per
+// MMA) need one.
 //
 // Warp roles (per token tile, see TcGemmCfg):
 //   warp 0       TMA producer: packed FP4 codes, ONE tensor-map box per
@@ -142,6 +143,13 @@ struct TcGemmCfg {
   // (token tiles in shared memory) have their own depths and barriers
   static constexpr int kStagesA = TN <= 64 ? 6 : 4;
   static constexpr int kStagesB = TN <= 64 ? 6 : (TN <= 128 ? 4 : 2);
+  // B units per stage.  2 rings the token rows of 256-token tiles in 128-K
+  // halves (a half refilled as soon as its 4 MMAs are done; K-chunk-major rows
+  // only); measured 2-3 % slower than whole stages (two more waits and
+  // commits per stage), so 1
+  static constexpr int kBSplit = 1;
+  static constexpr int kUnitBytes = kBBytes / kBSplit;
+  static constexpr int kUnitsB = kStagesB * kBSplit;
   // accumulator sets per issuer: two where TMEM has room, so the MMAs of the
   // next item do not wait for the epilogue of this one
   static constexpr int kAccSlots = kIssuers * 2 * kAccCols + kStagesA * 64 <= 512 ? 2 : 1;
@@ -165,7 +173,7 @@ struct TcGemmCfg {
   static constexpr int kOffBar = kOffMeta + kMetaSlots * kMetaBytes;
   // barriers: pk_full/empty[SP], a_full/empty[SA], b_full/empty[SB], acc_full/empty[2],
   // meta_full/empty[kMetaSlots], sh_full/empty[kShSlots]
-  static constexpr int kNumBars = 2 * kStagesP + 2 * kStagesA + 2 * kStagesB + 4 + 2 * kMetaSlots + 2 * kShSlots;
+  static constexpr int kNumBars = 2 * kStagesP + 2 * kStagesA + 2 * kUnitsB + 4 + 2 * kMetaSlots + 2 * kShSlots;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
@@ -176,7 +184,8 @@ struct TcGemmCfg {
   static constexpr int kThreads = kWarps * 32;
   static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "token tile");
   static_assert(kStagesA % kDecodeGroups == 0 && kStagesA % kIssuers == 0 &&
-                    kStagesB % kIssuers == 0 && kStagesB % 2 == 0,
+                    kStagesB % kIssuers == 0 && kStagesB % 2 == 0 &&
+                    (kBSplit == 1 || kIssuers == 1),
                 "ring discipline");
   static_assert(kStagesP % kDecodeGroups == 0 && kStagesP >= 3, "packed ring");
   static_assert(kAColBase + kStagesA * 64 <= kTmemCols, "TMEM budget");
@@ -220,7 +229,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   constexpr bool kBiased = (EPIF & kEpiBiased) != 0;
   using C = TcGemmCfg<TN>;
   constexpr int SA = C::kStagesA;
-  constexpr int SB = C::kStagesB;
+  constexpr int SB = C::kUnitsB;  // B ring units
+  constexpr int BU = C::kBSplit;  // B units per stage
   constexpr int SP = C::kStagesP;
   constexpr int AS = C::kAccSlots;
 
@@ -386,24 +396,29 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         for (int s = s_first; s < nks; s += C::kIssuers) {
           const uint32_t gs = g + s;
           const int sa = gs % SA;
-          const int sb = gs % SB;
           DSV4_TRACE_EV(9, gs);
-          mbar_wait(b_full(sb), (gs / SB) & 1, kErrWaitAbFull);
           mbar_wait(a_full(sa), (gs / SA) & 1, kErrWaitAbFull);
           DSV4_TRACE_EV(3, gs);
-          tc_fence_after();
           const uint32_t a_tmem = tmem + C::kAColBase + sa * 64;
-          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((sb * C::kBBytes) >> 4);
           const int nkb = stage_kb(ks0 + s);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            if (kk < nkb)
-              mma_i8_ts(d_tmem, a_tmem + kk * 8,
-                        bdesc + static_cast<uint64_t>(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4),
-                        idesc, (s > s_first || kk > 0) ? 1u : 0u);
+          for (int h = 0; h < BU; ++h) {
+            const uint32_t u = gs * BU + h;
+            const int sb = u % SB;
+            mbar_wait(b_full(sb), (u / SB) & 1, kErrWaitAbFull);
+            tc_fence_after();
+            const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((sb * C::kUnitBytes) >> 4);
+#pragma unroll
+            for (int kq = 0; kq < 8 / BU; ++kq) {
+              const int kk = h * (8 / BU) + kq;  // 32-K block of the stage
+              if (kk < nkb)
+                mma_i8_ts(d_tmem, a_tmem + kk * 8,
+                          bdesc + static_cast<uint64_t>(((kq >> 2) * C::kBHalf + (kq & 3) * 32) >> 4),
+                          idesc, (s > s_first || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(b_empty(sb));
           }
           mma_commit(a_empty(sa));
-          mma_commit(b_empty(sb));
           DSV4_TRACE_EV(6, gs);
         }
         mma_commit(acc_full(as));
@@ -431,6 +446,19 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           k_range(it, ks0, nks);
           const int row0 = p.moe ? it.b * p.block_m : it.b * TN;
           for (int s = 0; s < nks; ++s, ++g) {
+            if (BU == 2) {
+              // two 128-K units per stage, box {128, TN, 1} each
+#pragma unroll
+              for (int h = 0; h < BU; ++h) {
+                const uint32_t u = g * BU + h;
+                const int sb = u % SB;
+                mbar_wait(b_empty(sb), ((u / SB) & 1) ^ 1, kErrWaitAbEmpty);
+                const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kUnitBytes);
+                mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(C::kUnitBytes));
+                tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2 + h, b_full(sb), pol);
+              }
+              continue;
+            }
             const int sb = g % SB;
             mbar_wait(b_empty(sb), ((g / SB) & 1) ^ 1, kErrWaitAbEmpty);
             DSV4_TRACE_EV(7, g);
@@ -543,9 +571,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           // Warps 2 and 3 take alternate stages and gather only the rows up to
           // the last valid one (4 at a time, lane l -> rows 4l .. 4l+3 of both
           // 128-K halves); the MMA columns beyond are never stored.
+          // (one B unit per stage: 256-token tiles never run in gather4 mode)
           const int last = max(meta_last(ms)[0], meta_last(ms)[1]);
           const int n_rows = ((max(last, 0) + 4) / 4) * 4;
-          for (int s = 0; s < nks; ++s, ++g) {
+          for (int s = 0; s < nks && BU == 1; ++s, ++g) {
             if (static_cast<int>(g & 1) != warp - 2) continue;
             const int sb = g % SB;
             const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
