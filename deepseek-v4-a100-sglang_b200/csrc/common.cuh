@@ -323,6 +323,17 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Wait for outstanding tcgen05.ld with the destination registers tied to the
+// wait, so no use of them can be scheduled above it (for loads issued ahead).
+__device__ __forceinline__ void tmem_ld_wait_regs(int32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]),
+                 "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]),
+                 "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
+
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row atoms of
 // 8 x 128 B stacked every 1024 B (stride byte offset), version 1, layout
 // SWIZZLE_128B (2).  Start address must be 1024-aligned apart from the

@@ -629,16 +629,28 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       for (int q = 0; q < min(nks, C::kIssuers); ++q) accmask |= 1u << ((g + q) % C::kIssuers);
       const uint32_t t0 = tmem + (as * C::kIssuers) * C::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
       const float csn = EPI == kEpiI32 ? 0.f : meta_cs(ms)[row_local];
+      // One accumulator (kIssuers == 1, the 256-token tiles): the TMEM load of
+      // the next 16 columns is issued before this chunk is processed, so its
+      // latency overlaps the chunk's work.
+      int32_t pre[16];
+      if constexpr (C::kIssuers == 1) tmem_ld_x16(t0, pre);
       auto load16 = [&](int c0, int32_t (&v)[16]) {
 #pragma unroll
         for (int q = 0; q < 16; ++q) v[q] = kBiased ? rs_s[c0 + q] : 0;
-        for (int a = 0; a < C::kIssuers; ++a) {
-          if (!(accmask & (1u << a))) continue;
-          int32_t w[16];
-          tmem_ld_x16(t0 + a * C::kAccCols + c0, w);
-          tmem_ld_wait();
+        if constexpr (C::kIssuers == 1) {
+          tmem_ld_wait_regs(pre);
 #pragma unroll
-          for (int q = 0; q < 16; ++q) v[q] += w[q];
+          for (int q = 0; q < 16; ++q) v[q] += pre[q];
+          if (c0 + 16 < n_mma) tmem_ld_x16(t0 + c0 + 16, pre);
+        } else {
+          for (int a = 0; a < C::kIssuers; ++a) {
+            if (!(accmask & (1u << a))) continue;
+            int32_t w[16];
+            tmem_ld_x16(t0 + a * C::kAccCols + c0, w);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] += w[q];
+          }
         }
       };
 
