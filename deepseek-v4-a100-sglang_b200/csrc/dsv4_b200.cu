@@ -529,6 +529,41 @@ int dsv4_b200_remap_mxfp4_weight_for_int8(const uint8_t* weight, const uint8_t* 
   return check_launch("repack_codes_kernel");
 }
 
+int dsv4_b200_router_topk(const void* logits, int dtype, int64_t m, int64_t num_experts,
+                          const float* bias, int64_t topk, int renormalize, float scale,
+                          int32_t* topk_ids, float* topk_weights, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0 && m < (1ll << 31), "bad m %lld", (long long)m);
+  DSV4_REQUIRE(num_experts >= 1 && num_experts <= 1024, "num_experts must be in [1, 1024]");
+  DSV4_REQUIRE(topk >= 1 && topk <= 32 && topk <= num_experts, "topk must be in [1, min(32, E)]");
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(logits && topk_ids && topk_weights, "null pointer argument");
+  const int epl = static_cast<int>((num_experts + 31) / 32);
+  const dim3 grid(static_cast<unsigned>((m + 7) / 8));
+  cudaStream_t st = as_stream(stream);
+  const int e = static_cast<int>(num_experts), k = static_cast<int>(topk);
+#define DSV4_RT(T, EPL)                                                                       \
+  router_topk_kernel<T, EPL><<<grid, 256, 0, st>>>(static_cast<const T*>(logits), m, e, bias, k, \
+                                                   renormalize, scale, topk_ids, topk_weights)
+#define DSV4_RT_E(T)                                    \
+  if (epl <= 1) DSV4_RT(T, 1);                          \
+  else if (epl <= 2) DSV4_RT(T, 2);                     \
+  else if (epl <= 4) DSV4_RT(T, 4);                     \
+  else if (epl <= 8) DSV4_RT(T, 8);                     \
+  else if (epl <= 16) DSV4_RT(T, 16);                   \
+  else DSV4_RT(T, 32)
+  switch (dtype) {
+    case DSV4_F32: DSV4_RT_E(float); break;
+    case DSV4_F16: DSV4_RT_E(__half); break;
+    case DSV4_BF16: DSV4_RT_E(__nv_bfloat16); break;
+    default:
+      return fail(DSV4_ERR_INVALID_ARGUMENT, "logits must be fp32, fp16, or bf16 (dtype %d)", dtype);
+  }
+#undef DSV4_RT_E
+#undef DSV4_RT
+  return check_launch("router_topk_kernel");
+}
+
 int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int64_t num_experts,
                                    int64_t block_size, int32_t* sorted_token_ids,
                                    int64_t sorted_capacity, int32_t* expert_ids,

@@ -219,6 +219,69 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
 }
 
 // ---------------------------------------------------------------------------
+// Router top-k (the DeepSeek routing SGLang computes before the MoE call,
+// reference PATCH:505-507): score = sigmoid(logit); the top-k experts by
+// score + bias (bias used for selection only); weight = chosen score,
+// renormalised to sum 1 when asked, times `scale`.  One warp per token, EPL
+// experts per lane in registers; k rounds of a warp argmax (ties: lower
+// expert index), so the k results come out in descending order.
+template <typename T, int EPL>
+__global__ void __launch_bounds__(256) router_topk_kernel(const T* __restrict__ logits, int64_t m,
+                                                          int e, const float* __restrict__ bias,
+                                                          int topk, int renormalize, float scale,
+                                                          int32_t* __restrict__ ids,
+                                                          float* __restrict__ weights) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= m) return;
+  float sel[EPL], sc[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int x = j * 32 + lane;
+    if (x < e) {
+      const float l = to_f32<T>(logits[row * e + x]);
+      sc[j] = 1.0f / (1.0f + expf(-l));
+      sel[j] = sc[j] + (bias != nullptr ? bias[x] : 0.f);
+    } else {
+      sc[j] = 0.f;
+      sel[j] = -INFINITY;
+    }
+  }
+  float wsum = 0.f, my_w = 0.f;
+  int my_id = -1;
+  for (int r = 0; r < topk; ++r) {
+    float bv = -INFINITY;
+    int bx = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int x = j * 32 + lane;
+      if (sel[j] > bv || (sel[j] == bv && x < bx)) bv = sel[j], bx = x;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int ox = __shfl_xor_sync(0xffffffffu, bx, o);
+      if (ov > bv || (ov == bv && ox < bx)) bv = ov, bx = ox;
+    }
+    // the owning lane clears the winner and broadcasts its score
+    float w = 0.f;
+    if ((bx & 31) == lane) {
+#pragma unroll
+      for (int j = 0; j < EPL; ++j)
+        if (j == (bx >> 5)) w = sc[j], sel[j] = -INFINITY;
+    }
+    w = __shfl_sync(0xffffffffu, w, bx & 31);
+    wsum += w;
+    if (lane == r) my_w = w, my_id = bx;
+  }
+  if (lane < topk) {
+    const float w = renormalize ? my_w / wsum : my_w;
+    ids[row * topk + lane] = my_id;
+    weights[row * topk + lane] = w * scale;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // a5. expert align (reference call site PYMOE:842-869, library
 // sgl_kernel.moe_align_block_size).  One CTA of 1024 threads:
 //   1. each warp owns a contiguous segment of the flattened ids and counts

@@ -17,6 +17,7 @@ from .mxfp4_int8_moe import (  # noqa: F401
     remap_mxfp4_weight_for_int8,
     select_mxfp4_int8_moe_tile_shape,
     select_sorted_block_m,
+    router_topk,
 )
 from .jit_ops import (  # noqa: F401
     mxfp4_int8_dense_gemm,

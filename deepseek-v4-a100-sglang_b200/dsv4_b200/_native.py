@@ -39,6 +39,7 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_mxfp4_int8_moe_gemm_swiglu": [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64,
                                              _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I,
                                              _F, _P],
+    "dsv4_b200_router_topk": [_P, _I, _I64, _I64, _P, _I64, _I, _F, _P, _P, _P],
     "dsv4_b200_moe_sort_rows": [_P, _P, _I64, _I64, _P, _I64, _P, _I64, _I, _I64, _P, _P, _P,
                                 _P],
     "dsv4_b200_quantize_sorted_int8": [_P, _I, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P],

@@ -239,6 +239,31 @@ def select_sorted_block_m(m: int, topk: int, experts: int) -> int:
     return block_m
 
 
+def router_topk(router_logits: torch.Tensor, topk: int, *, bias: torch.Tensor | None = None,
+                renormalize: bool = True, scale: float = 1.0):
+    """DeepSeek routing on the GPU (what SGLang computes before the MoE call,
+    PATCH:505-507): sigmoid scores, top-``topk`` experts by score + ``bias``
+    (selection only), weights = chosen scores renormalised (and scaled).
+    Returns ``(topk_ids int32 [M, topk], topk_weights fp32 [M, topk])`` in
+    descending order, ready for :func:`moe_align_block_size`."""
+    if router_logits.dim() != 2 or router_logits.dtype not in _DTYPES:
+        raise ValueError("router_logits must be a 2-D fp32/fp16/bf16 tensor")
+    _require_cuda(router_logits, "router_logits")
+    logits = router_logits.contiguous()
+    m, e = logits.shape
+    b = None
+    if bias is not None:
+        b = bias.to(device=logits.device, dtype=torch.float32).contiguous()
+        if b.shape != (e,):
+            raise ValueError(f"bias must have shape [{e}], got {tuple(b.shape)}")
+    ids = torch.empty((m, topk), device=logits.device, dtype=torch.int32)
+    w = torch.empty((m, topk), device=logits.device, dtype=torch.float32)
+    N.call("dsv4_b200_router_topk", logits.data_ptr(), _DTYPES[logits.dtype], m, e,
+           b.data_ptr() if b is not None else None, topk, 1 if renormalize else 0, float(scale),
+           ids.data_ptr(), w.data_ptr(), N.stream_of(logits))
+    return ids, w
+
+
 def align_capacity(numel: int, num_experts: int, block_size: int) -> int:
     """PYMOE:848-851."""
     if numel < num_experts + 1:

@@ -81,6 +81,18 @@ DSV4_API int dsv4_b200_remap_mxfp4_weight_for_int8(const uint8_t* weight, const 
                                           uint8_t* b_mxfp4, uint8_t* b_shift2,
                                           float* channel_scale, void* stream);
 
+/* Router top-k (the routing SGLang computes before the MoE call, reference
+ * PATCH:505-507, DeepSeek sigmoid + bias): score = sigmoid(logit) in fp32;
+ * topk_ids[t][0..topk) = the experts with the largest score + bias[e] (bias
+ * may be NULL; it selects only), in descending order, ties to the lower
+ * expert; topk_weights = their scores, divided by their sum when
+ * renormalize != 0, times scale.  logits [m][num_experts] fp32/fp16/bf16;
+ * num_experts <= 1024, topk <= 32.  Its output feeds
+ * dsv4_b200_moe_align_block_size. */
+DSV4_API int dsv4_b200_router_topk(const void* logits, int dtype, int64_t m, int64_t num_experts,
+                                   const float* bias, int64_t topk, int renormalize, float scale,
+                                   int32_t* topk_ids, float* topk_weights, void* stream);
+
 /* a5. Expert histogram + block-padded prefix sum + stable permutation.
  * Replaces the sgl_kernel.moe_align_block_size call of
  * _moe_align_block_size (PYMOE:842-869).  topk_ids int32 [numel]; experts

@@ -266,6 +266,66 @@ def test_moe_forward_matches_reference_golden(golden):
     assert O.relative_l2(out.float().cpu().numpy(), O.bf16_bits_to_f32(ref2)) < 1e-2
 
 
+@pytest.mark.parametrize("m,e,topk,dtype", [(64, 256, 8, torch.float32),
+                                             (1000, 256, 8, torch.float32),
+                                             (37, 16, 4, torch.float32),
+                                             (5, 1000, 12, torch.float32),
+                                             (200, 256, 8, torch.bfloat16)])
+def test_router_topk_matches_torch(m, e, topk, dtype):
+    """Device routing vs the torch DeepSeek routing the benchmark uses: same
+    experts in the same order; weights to fp32 rounding (expf and the order
+    of the renormalising sum differ)."""
+    gen = torch.Generator().manual_seed(m * 7 + e)
+    logits = (torch.randn(m, e, generator=gen) * 2).to(dtype)
+    bias = torch.randn(e, generator=gen) * 0.1
+    scores = torch.sigmoid(logits.float())
+    _, ref_ids = torch.topk(scores + bias[None, :], topk, dim=-1)
+    ref_w = torch.gather(scores, 1, ref_ids)
+    ref_w = ref_w / ref_w.sum(-1, keepdim=True) * 2.5
+    ids, w = D.router_topk(logits.to(DEV), topk, bias=bias.to(DEV), scale=2.5)
+    ids2, w2 = D.router_topk(logits.to(DEV), topk, renormalize=False)
+    _, ref2 = torch.topk(scores, topk, dim=-1)
+    # the chosen selection values are the top-k values, in order
+    sel = (scores + bias[None, :])
+    np.testing.assert_allclose(torch.gather(sel, 1, ids.cpu().long()).numpy(),
+                               torch.gather(sel, 1, ref_ids).numpy(), rtol=1e-6)
+    np.testing.assert_allclose(torch.gather(scores, 1, ids2.cpu().long()).numpy(),
+                               torch.gather(scores, 1, ref2).numpy(), rtol=1e-6)
+    if dtype == torch.float32:  # no exact ties: the same experts, same order
+        np.testing.assert_array_equal(ids.cpu().numpy(), ref_ids.numpy())
+        np.testing.assert_allclose(w.cpu().numpy(), ref_w.numpy(), rtol=2e-6, atol=1e-7)
+        np.testing.assert_array_equal(ids2.cpu().numpy(), ref2.numpy())
+        np.testing.assert_allclose(w2.cpu().numpy(), torch.gather(scores, 1, ref2).numpy(),
+                                   rtol=2e-6)
+    else:  # bf16 logits tie often; ties go to the lower expert index here
+        s_ids = torch.gather(sel, 1, ids.cpu().long())
+        assert bool((s_ids[:, :-1] >= s_ids[:, 1:]).all())
+
+
+def test_sglang_hook_matches_forward(golden):
+    """The SGLang hook (PATCH:450-581) prepares the layer and returns exactly
+    mxfp4_int8_moe_forward's output, with the config's scaling and clamp."""
+    import types
+    import dsv4_b200.sglang_hook as H
+    g = golden("moe_ref_small")
+    layer = torch.nn.Module()
+    for nm, key in (("w13_weight", "w13"), ("w2_weight", "w2"),
+                    ("w13_weight_scale_inv", "s13"), ("w2_weight_scale_inv", "s2")):
+        setattr(layer, nm, torch.nn.Parameter(torch.from_numpy(g[key]).to(DEV), requires_grad=False))
+    cfg = types.SimpleNamespace(num_experts_per_tok=2, routed_scaling_factor=1.5, swiglu_limit=7.0)
+    method = types.SimpleNamespace(runner=types.SimpleNamespace(config=cfg))
+    H.process_weights_after_loading(method, layer)
+    x = torch.from_numpy(g["hidden_bits"]).view(torch.bfloat16).to(DEV)
+    ids = torch.from_numpy(g["topk_ids"]).to(DEV)
+    tw = torch.from_numpy(g["topk_weights"]).to(DEV)
+    topk = types.SimpleNamespace(topk_ids=ids, topk_weights=tw)
+    out = H.apply(method, layer, types.SimpleNamespace(hidden_states=x, topk_output=topk))
+    ref = D.mxfp4_int8_moe_forward(x, layer._dsv4_mxfp4_int8_weights, ids, tw, hidden_size=128,
+                                   intermediate_size=128, routed_scaling_factor=1.5,
+                                   clamp_limit=7.0)
+    assert torch.equal(out.hidden_states, ref)
+
+
 def test_moe_forward_config1_matches_reference_golden(golden):
     g = golden("moe_ref_config1")
     e, t, h, i, topk = 8, 16, 1024, 512, 2
