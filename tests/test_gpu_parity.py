@@ -95,7 +95,7 @@ def test_dense_i32_bit_exact(m, n, k):
 
 @pytest.mark.parametrize("m,n,k", [(1, 256, 1024), (16, 256, 1024), (100, 256, 1024),
                                    (128, 256, 1024), (300, 256, 1024), (7, 1024, 7168),
-                                   (520, 384, 2304)])
+                                   (520, 384, 2304), (300, 256, 5120)])
 def test_dense_bf16_bit_exact(m, n, k):
     _, (b, sh, cs), (db, dsh, dcs) = _weights(1, n, k, 77 + m)
     x = G.randn_bf16((m, k), 5 + m)
@@ -129,7 +129,9 @@ MOE_CASES = [(4, 13, 128, 128, 2, 16), (16, 64, 256, 128, 8, 16), (8, 40, 256, 2
              (8, 300, 128, 128, 2, 64), (8, 600, 128, 128, 2, 128),
              # long pipelines: many 256-K stages per item and many items per CTA
              (16, 64, 2048, 256, 8, 16), (8, 96, 1536, 384, 4, 32), (8, 256, 1152, 256, 4, 64),
-             (4, 512, 1024, 256, 2, 128)]
+             (4, 512, 1024, 256, 2, 128),
+             # 17 stages: crosses a 16-stage shift chunk on the 128-token tile
+             (4, 260, 4352, 128, 2, 128)]
 
 
 @pytest.mark.parametrize("case", MOE_CASES)
@@ -179,7 +181,7 @@ def _cm_rows(t, cap, k):  # K-chunk-major [k/128][cap][128] -> [cap][k]
 
 # the sorted path also runs 256-token tiles (N=256 MMAs, one issuer)
 SORTED_CASES = MOE_CASES + [(8, 1200, 256, 256, 2, 256), (4, 640, 1024, 256, 4, 256),
-                            (16, 300, 512, 128, 8, 256)]
+                            (16, 300, 512, 128, 8, 256), (4, 600, 4352, 128, 2, 256)]
 
 
 @pytest.mark.parametrize("case", SORTED_CASES)
