@@ -204,8 +204,8 @@ int encode_weight_maps(TcGemmParams& p, const uint8_t* b_mxfp4, const uint8_t* b
   return DSV4_OK;
 }
 
-int shift_chunk_rows(int stages_per_item) {
-  const int c = TcGemmCfg<16>::kShChunk;
+int shift_chunk_rows(int stages_per_item, int tn) {
+  const int c = tn >= 256 ? TcGemmCfg<256>::kShChunk : TcGemmCfg<16>::kShChunk;
   return 2 * (stages_per_item < c ? stages_per_item : c);
 }
 
@@ -325,7 +325,7 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   p.has_clamp = has_clamp;
   p.clamp_limit = clamp_limit;
   if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, experts, k / 32, shift_stride, n_rows / 8,
-                                 epi == kEpiSwiglu, inter, shift_chunk_rows(p.k_stages)))
+                                 epi == kEpiSwiglu, inter, shift_chunk_rows(p.k_stages, static_cast<int>(block_m))))
     return r;
   if (int r = encode_act_map(p, a_q, m_in, k, sorted_rows ? 2 : 0, static_cast<int>(block_m)))
     return r;
@@ -377,7 +377,7 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   p.split_stride = split_stride;
   const int tn = dense_tile(m);
   if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, 1, k / 32, shift_stride, n / 8, false, 0,
-                                 shift_chunk_rows(p.stages_per_split)))
+                                 shift_chunk_rows(p.stages_per_split, tn)))
     return r;
   if (int r = encode_act_map(p, a_q, m, k, 1, tn)) return r;
   p.m_tiles = static_cast<int>((m + tn - 1) / tn);

@@ -128,7 +128,7 @@ struct TcGemmCfg {
   static constexpr int kPBytes = 128 * 256 / 2;  // packed FP4 codes of one 256-K stage
   // shift chunks: the 2-bit shifts of kShChunk stages, [2 * kShChunk rows][128 B]
   // (row = one 4-block shift word per output row; SwiGLU: gate 64 B | up 64 B)
-  static constexpr int kShChunk = 32;
+  static constexpr int kShChunk = TN >= 256 ? 16 : 32;  // (256-token tiles: smem is full)
   static constexpr int kShSlotBytes = 2 * kShChunk * 128;
   static constexpr int kShSlots = TN <= 64 ? 4 : 2;  // chunks in flight (short-K items: one each)
   static constexpr int kAccCols = TN;                     // N columns per accumulator
@@ -138,7 +138,13 @@ struct TcGemmCfg {
   // (256-token tiles: an N=256 MMA takes 128 tensor cycles, more than its
   // issue cost, so one issuer keeps the tensor pipe busy)
   static constexpr int kIssuers = TN <= 16 ? 3 : (TN <= 128 ? 2 : 1);
-  static constexpr int kDecodeGroups = TN <= 64 ? 3 : 4;  // groups of 4 decode warps
+  // groups of 4 decode warps (256-token tiles need a decoded stage per ~1000
+  // cycles, which 8 warps deliver; their threads go to a second epilogue group)
+  static constexpr int kDecodeGroups = TN <= 64 ? 3 : (TN <= 128 ? 4 : 2);
+  // epilogue warps: 4, or 8 for 256-token tiles (two groups of 4 take
+  // alternate 16-column chunks: that epilogue cannot overlap the next item's
+  // MMAs, so its length counts in full)
+  static constexpr int kEpiWarps = TN >= 256 ? 8 : 4;
   // A ring (decoded weights in TMEM, 64 columns = 256 K per slot) and B ring
   // (token tiles in shared memory) have their own depths and barriers
   static constexpr int kStagesA = TN <= 64 ? 6 : 4;
@@ -156,7 +162,8 @@ struct TcGemmCfg {
   // TMEM (512 columns): [issuer accumulators], then 64-column A slots
   static constexpr int kAColBase = kIssuers * kAccSlots * kAccCols;
   static constexpr int kTmemCols = 512;
-  static constexpr int kStgBytes = 16 * 128 * 2;   // SwiGLU staging (16 cols x 128 rows bf16)
+  // epilogue staging, per epilogue group: 16 token columns x 128 rows bf16
+  static constexpr int kStgBytes = (kEpiWarps / 4) * 16 * 128 * 2;
   // src, orow, ascale, rowsum [TN]; per-warp last [4]; channel scales [128]
   static constexpr int kMetaBytes = TN * 16 + 16 + 512;
   static constexpr int kMetaSlots = TN <= 128 ? 4 : 2;  // items of metadata prepared ahead
@@ -177,9 +184,10 @@ struct TcGemmCfg {
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
-  // warps: 0 TMA, 1 issuer 0 + TMEM, 2-3 gather, 4-7 epilogue, decode groups, issuers 1..
+  // warps: 0 TMA, 1 issuer 0 + TMEM, 2-3 gather, epilogue, decode groups, issuers 1..
   static constexpr int kDecodeWarps = 4 * kDecodeGroups;
-  static constexpr int kIssuer1Warp = 8 + kDecodeWarps;
+  static constexpr int kDecBase = 4 + kEpiWarps;
+  static constexpr int kIssuer1Warp = kDecBase + kDecodeWarps;
   static constexpr int kWarps = kIssuer1Warp + kIssuers - 1;
   static constexpr int kThreads = kWarps * 32;
   static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "token tile");
@@ -293,7 +301,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(acc_full(s), C::kIssuers);
-      mbar_init(acc_empty(s), 4);
+      mbar_init(acc_empty(s), C::kEpiWarps);
     }
     for (int s = 0; s < SHS; ++s) {
       mbar_init(sh_full(s), 1);
@@ -302,7 +310,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     for (int s = 0; s < MS; ++s) {
       // metadata warps (two, or one in the tiled modes) + the channel-scale copy
       mbar_init(meta_full(s), p.b_mode != 0 ? 2 : 3);
-      mbar_init(meta_empty(s), 4);
+      mbar_init(meta_empty(s), C::kEpiWarps);
     }
     mbar_fence_init();
   }
@@ -601,12 +609,15 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         ++t;
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < C::kDecBase) {
     // -------------------------------- epilogue --------------------------------
+    constexpr int EH = C::kEpiWarps / 4;  // epilogue groups: group eh takes chunks eh, eh + EH, ..
+    const int eh = (warp - 4) >> 2;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     const int row_local = quarter * 32 + lane;
-    const int e = tid - 128;       // 0..127
-    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg);
+    const int e = row_local;       // 0..127 within the group
+    const int ebar = eh == 0 ? 1 : 3;  // named barrier of the group (2 is the gather warps')
+    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg) + eh * (16 * 128);
     const float lim = p.has_clamp ? __bfloat162float(f2bf(p.clamp_limit)) : 0.f;
     uint32_t t = 0, g = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
@@ -633,7 +644,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       // the next 16 columns is issued before this chunk is processed, so its
       // latency overlaps the chunk's work.
       int32_t pre[16];
-      if constexpr (C::kIssuers == 1) tmem_ld_x16(t0, pre);
+      if constexpr (C::kIssuers == 1) tmem_ld_x16(t0 + 16 * eh, pre);
       auto load16 = [&](int c0, int32_t (&v)[16]) {
 #pragma unroll
         for (int q = 0; q < 16; ++q) v[q] = kBiased ? rs_s[c0 + q] : 0;
@@ -641,7 +652,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           tmem_ld_wait_regs(pre);
 #pragma unroll
           for (int q = 0; q < 16; ++q) v[q] += pre[q];
-          if (c0 + 16 < n_mma) tmem_ld_x16(t0 + c0 + 16, pre);
+          if (c0 + 16 * EH < n_mma) tmem_ld_x16(t0 + c0 + 16 * EH, pre);
         } else {
           for (int a = 0; a < C::kIssuers; ++a) {
             if (!(accmask & (1u << a))) continue;
@@ -656,7 +667,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
 
       if (EPI == kEpiSwiglu) {
         const int j0 = it.y * 64;
-        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
           int32_t v[16];
           load16(c0, v);
 #pragma unroll
@@ -664,7 +675,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             const float x = __fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn);
             stg[q * 128 + row_local] = f2bf(x);
           }
-          named_bar_sync(1, 128);
+          named_bar_sync(ebar, 128);
           const int col = c0 + (e >> 3);
           const int i0 = (e & 7) * 8;
           const int orow = orow_s[col];
@@ -687,11 +698,11 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo + j0 + i0) =
                 *reinterpret_cast<const uint4*>(h);
           }
-          named_bar_sync(1, 128);
+          named_bar_sync(ebar, 128);
         }
       } else {
         const int n_g = it.y * 128 + row_local;
-        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
           int32_t v[16];
           load16(c0, v);
           if (EPI == kEpiBf16) {
@@ -702,7 +713,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             for (int q = 0; q < 16; ++q)
               stg[q * 128 + row_local] =
                   f2bf(__fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn));
-            named_bar_sync(1, 128);
+            named_bar_sync(ebar, 128);
             const int col = e >> 3;         // token of the chunk
             const int ch0 = (e & 7) * 16;   // 16 channels
             const int orow = orow_s[c0 + col];
@@ -713,7 +724,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
               dst[0] = src[0];
               dst[1] = src[1];
             }
-            named_bar_sync(1, 128);
+            named_bar_sync(ebar, 128);
           } else {
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
@@ -741,7 +752,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     // lane quarter w % 4 (rows 32*(w%4) ..) and all 8 32-K blocks of the stage
     // (64 TMEM columns: block kb -> columns 8kb .. 8kb+7).
     const int quarter = warp & 3;
-    const int grp = (warp - 8) >> 2;
+    const int grp = (warp - C::kDecBase) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16, one = p.dec_one;
