@@ -646,8 +646,16 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       int32_t pre[16];
       if constexpr (C::kIssuers == 1) tmem_ld_x16(t0 + 16 * eh, pre);
       auto load16 = [&](int c0, int32_t (&v)[16]) {
+        if (kBiased) {  // row-sum corrections of the 16 tokens, 4 vector loads
 #pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = kBiased ? rs_s[c0 + q] : 0;
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int4 r = reinterpret_cast<const int4*>(rs_s + c0)[q4];
+            v[4 * q4] = r.x, v[4 * q4 + 1] = r.y, v[4 * q4 + 2] = r.z, v[4 * q4 + 3] = r.w;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) v[q] = 0;
+        }
         if constexpr (C::kIssuers == 1) {
           tmem_ld_wait_regs(pre);
 #pragma unroll
@@ -665,16 +673,35 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         }
       };
 
+      // bf16((f32(acc) * a_scale) * cs) of the 16 tokens into the staging
+      // tile [token][128 rows]: scales by vector loads, rounding two values
+      // per conversion (the same round-to-nearest-even per value)
+      auto stage16 = [&](int c0, const int32_t (&v)[16]) {
+        uint16_t* sbs = reinterpret_cast<uint16_t*>(stg);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 a = reinterpret_cast<const float4*>(asc_s + c0)[q4];
+          const float x0 = __fmul_rn(__fmul_rn(__int2float_rn(v[4 * q4]), a.x), csn);
+          const float x1 = __fmul_rn(__fmul_rn(__int2float_rn(v[4 * q4 + 1]), a.y), csn);
+          const float x2 = __fmul_rn(__fmul_rn(__int2float_rn(v[4 * q4 + 2]), a.z), csn);
+          const float x3 = __fmul_rn(__fmul_rn(__int2float_rn(v[4 * q4 + 3]), a.w), csn);
+          const __nv_bfloat162 p01 = __floats2bfloat162_rn(x0, x1);
+          const __nv_bfloat162 p23 = __floats2bfloat162_rn(x2, x3);
+          const uint32_t u01 = *reinterpret_cast<const uint32_t*>(&p01);
+          const uint32_t u23 = *reinterpret_cast<const uint32_t*>(&p23);
+          sbs[(4 * q4) * 128 + row_local] = static_cast<uint16_t>(u01);
+          sbs[(4 * q4 + 1) * 128 + row_local] = static_cast<uint16_t>(u01 >> 16);
+          sbs[(4 * q4 + 2) * 128 + row_local] = static_cast<uint16_t>(u23);
+          sbs[(4 * q4 + 3) * 128 + row_local] = static_cast<uint16_t>(u23 >> 16);
+        }
+      };
+
       if (EPI == kEpiSwiglu) {
         const int j0 = it.y * 64;
         for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
           int32_t v[16];
           load16(c0, v);
-#pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const float x = __fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn);
-            stg[q * 128 + row_local] = f2bf(x);
-          }
+          stage16(c0, v);
           named_bar_sync(ebar, 128);
           const int col = c0 + (e >> 3);
           const int i0 = (e & 7) * 8;
@@ -709,10 +736,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             // staged through shared memory ([token][128 channels] bf16) so a
             // thread stores 32 contiguous bytes of one token row instead of
             // 16 scattered 2-byte values
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-              stg[q * 128 + row_local] =
-                  f2bf(__fmul_rn(__fmul_rn(__int2float_rn(v[q]), asc_s[c0 + q]), csn));
+            stage16(c0, v);
             named_bar_sync(ebar, 128);
             const int col = e >> 3;         // token of the chunk
             const int ch0 = (e & 7) * 16;   // 16 channels
