@@ -707,23 +707,32 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           const int i0 = (e & 7) * 8;
           const int orow = orow_s[col];
           if (orow >= 0) {
-            __align__(16) __nv_bfloat16 h[8];
+            // 8 gate and 8 up values of token col, rows i0 .. i0+7 (16-byte reads)
+            const uint4 gq = *reinterpret_cast<const uint4*>(stg + (e >> 3) * 128 + i0);
+            const uint4 uq = *reinterpret_cast<const uint4*>(stg + (e >> 3) * 128 + 64 + i0);
+            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gq);
+            const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uq);
+            uint4 hq;
+            uint32_t* h2 = reinterpret_cast<uint32_t*>(&hq);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              float gv = __bfloat162float(stg[(e >> 3) * 128 + i0 + u]);
-              float up = __bfloat162float(stg[(e >> 3) * 128 + 64 + i0 + u]);
+            for (int u = 0; u < 4; ++u) {  // two rows per step, rounded as a pair
+              float2 gv = __bfloat1622float2(g2[u]);
+              float2 up = __bfloat1622float2(u2[u]);
               if (p.has_clamp) {
-                gv = fminf(gv, lim);
-                up = fminf(fmaxf(up, -lim), lim);
+                gv.x = fminf(gv.x, lim), gv.y = fminf(gv.y, lim);
+                up.x = fminf(fmaxf(up.x, -lim), lim), up.y = fminf(fmaxf(up.y, -lim), lim);
               }
               // silu in fast fp32 (MUFU exp2 / reciprocal): the result is
               // rounded to bf16, where it differs from the IEEE-exact form by
               // at most one ulp, and rarely
-              const float sg = __bfloat162float(f2bf(__fdividef(gv, 1.0f + __expf(-gv))));
-              h[u] = f2bf(__fmul_rn(sg, up));
+              const float2 sg = __bfloat1622float2(
+                  __floats2bfloat162_rn(__fdividef(gv.x, 1.0f + __expf(-gv.x)),
+                                        __fdividef(gv.y, 1.0f + __expf(-gv.y))));
+              const __nv_bfloat162 hh =
+                  __floats2bfloat162_rn(__fmul_rn(sg.x, up.x), __fmul_rn(sg.y, up.y));
+              h2[u] = *reinterpret_cast<const uint32_t*>(&hh);
             }
-            *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo + j0 + i0) =
-                *reinterpret_cast<const uint4*>(h);
+            *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo + j0 + i0) = hq;
           }
           named_bar_sync(ebar, 128);
         }
