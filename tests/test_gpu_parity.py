@@ -49,6 +49,30 @@ def test_quant_vs_oracle(m, k):
     np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), os_.view(np.uint32))
 
 
+@pytest.mark.parametrize("scale", [1.0, 3.0, 0.0078125, 0.37, 1e-3, 12345.0])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_quant_ties_bit_exact(scale, dtype):
+    """Rows built so that many x / s land on or next to half-integers, where
+    round-half-even decides: amax = 127 * scale, values scale * (k + 0.5)
+    and neighbours."""
+    if dtype == torch.float16 and 127 * scale > 60000:
+        pytest.skip("beyond the fp16 range")
+    k = 2048
+    base = (torch.arange(k) % 255 - 127).float()
+    rows = [base + 0.5, base - 0.5, base + 0.49999, base + 0.50001]
+    x = torch.stack([r.clamp(-127, 127) for r in rows] + [base]) * scale
+    x[:, 0] = 127 * scale  # pin amax
+    x = x.to(dtype)
+    q, qs = O.quantize_per_token_int8(x.float().numpy())
+    dq, dqs = D.quantize_per_token_int8(x.to(DEV))
+    np.testing.assert_array_equal(dq.cpu().numpy(), q)
+    np.testing.assert_array_equal(dqs.cpu().numpy(), qs)
+    xw = torch.cat([x, x], dim=1)  # K = 4096: the 128-thread row path
+    q2, _ = O.quantize_per_token_int8(xw.float().numpy())
+    dq2, _ = D.quantize_per_token_int8(xw.to(DEV))
+    np.testing.assert_array_equal(dq2.cpu().numpy(), q2)
+
+
 @pytest.mark.parametrize("name", ["repack_span3", "repack_baseline", "repack_wide"])
 @pytest.mark.parametrize("variant", ["tri", "torch"])
 def test_repack_golden(golden, name, variant):
