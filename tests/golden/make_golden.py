@@ -3,7 +3,7 @@
 Run in a container where the reference checkout is present (it is not on the
 GPU box; the committed .npz files travel instead):
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [REFERENCE_ROOT]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py REFERENCE_ROOT
 
 * ``dsv4_a100_patch/triton_kernels/mxfp4_int8_moe.py`` is loaded standalone
   with importlib (its package __init__ needs SGLang).  Its CPU torch quantiser,
@@ -65,7 +65,10 @@ def sha(*arrays) -> str:
 
 
 def main():
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DSV4_REFERENCE_ROOT")
+    if not arg:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (or set DSV4_REFERENCE_ROOT)")
+    root = Path(arg)
     ref, helpers = load_reference(root)
     out = {}
 
