@@ -225,9 +225,7 @@ int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, in
     DSV4_REQUIRE(k % 128 == 0, "K-chunk-major rows need K %% 128 == 0");
     cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(k / 128)};
     cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(rows) * 128};
-    // (box depth 2 / kBSplit: both 128-K halves of a stage per copy)
-    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(tn),
-                         static_cast<cuuint32_t>(tn >= 256 ? 2 / TcGemmCfg<256>::kBSplit : 2)};
+    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(tn), 2};
     r = encode_u8(&p.map_act, 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   } else {

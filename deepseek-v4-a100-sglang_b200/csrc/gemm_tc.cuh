@@ -121,6 +121,8 @@ struct TcGemmParams {
 //   decode group  g % kDecodeGroups   -> kDecodeGroups | kStagesA, kStagesP
 //   MMA issuer    g % kIssuers        -> kIssuers | kStagesA, kStagesB
 //   gather warp   g % 2               -> 2 | kStagesB
+//   token loader  waits for stage g - kStagesB on its A-slot empty barrier
+//                 (safe while kStagesA >= kStagesB, see TcGemmCfg)
 template <int TN>
 struct TcGemmCfg {
   static constexpr int kBHalf = TN * 128;        // one 128-K SW128 sub-tile of B
@@ -149,13 +151,13 @@ struct TcGemmCfg {
   // (token tiles in shared memory) have their own depths and barriers
   static constexpr int kStagesA = TN <= 64 ? 6 : 4;
   static constexpr int kStagesB = TN <= 64 ? 6 : (TN <= 128 ? 4 : 2);
-  // B units per stage.  2 rings the token rows of 256-token tiles in 128-K
-  // halves (a half refilled as soon as its 4 MMAs are done; K-chunk-major rows
-  // only); measured 2-3 % slower than whole stages (two more waits and
-  // commits per stage), so 1
-  static constexpr int kBSplit = 1;
-  static constexpr int kUnitBytes = kBBytes / kBSplit;
-  static constexpr int kUnitsB = kStagesB * kBSplit;
+  // One barrier pair per stage for both operands: the token-tile loader
+  // arrives (with its bytes) on the A slot's ready barrier, and reuses B slot
+  // g % kStagesB once the A-slot empty barrier shows stage g - kStagesB done.
+  // Safe for parity waits because kStagesA >= kStagesB: when the loader waits
+  // for stage g - kStagesB, every stage <= g - 1 - kStagesB is done already,
+  // so the slot is never two phases behind, and the slot's previous ready
+  // phase (stage g - kStagesA) has completed before the loader arrives.
   // accumulator sets per issuer: two where TMEM has room, so the MMAs of the
   // next item do not wait for the epilogue of this one
   static constexpr int kAccSlots = kIssuers * 2 * kAccCols + kStagesA * 64 <= 512 ? 2 : 1;
@@ -178,9 +180,9 @@ struct TcGemmCfg {
   static constexpr int kOffStg = kOffSh + kShSlots * kShSlotBytes;
   static constexpr int kOffMeta = kOffStg + kStgBytes;
   static constexpr int kOffBar = kOffMeta + kMetaSlots * kMetaBytes;
-  // barriers: pk_full/empty[SP], a_full/empty[SA], b_full/empty[SB], acc_full/empty[2],
+  // barriers: pk_full/empty[SP], a_full/empty[SA], acc_full/empty[2],
   // meta_full/empty[kMetaSlots], sh_full/empty[kShSlots]
-  static constexpr int kNumBars = 2 * kStagesP + 2 * kStagesA + 2 * kUnitsB + 4 + 2 * kMetaSlots + 2 * kShSlots;
+  static constexpr int kNumBars = 2 * kStagesP + 2 * kStagesA + 4 + 2 * kMetaSlots + 2 * kShSlots;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kSmemLaunch = kBytes + 1024;  // slack for 1024-B alignment
@@ -192,8 +194,7 @@ struct TcGemmCfg {
   static constexpr int kThreads = kWarps * 32;
   static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "token tile");
   static_assert(kStagesA % kDecodeGroups == 0 && kStagesA % kIssuers == 0 &&
-                    kStagesB % kIssuers == 0 && kStagesB % 2 == 0 &&
-                    (kBSplit == 1 || kIssuers == 1),
+                    kStagesB % kIssuers == 0 && kStagesB % 2 == 0 && kStagesA >= kStagesB,
                 "ring discipline");
   static_assert(kStagesP % kDecodeGroups == 0 && kStagesP >= 3, "packed ring");
   static_assert(kAColBase + kStagesA * 64 <= kTmemCols, "TMEM budget");
@@ -237,8 +238,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   constexpr bool kBiased = (EPIF & kEpiBiased) != 0;
   using C = TcGemmCfg<TN>;
   constexpr int SA = C::kStagesA;
-  constexpr int SB = C::kUnitsB;  // B ring units
-  constexpr int BU = C::kBSplit;  // B units per stage
+  constexpr int SB = C::kStagesB;
   constexpr int SP = C::kStagesP;
   constexpr int AS = C::kAccSlots;
 
@@ -265,9 +265,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   auto pk_empty = [&](int s) { return bar0 + 8u * (SP + s); };
   auto a_full = [&](int s) { return bar0 + 8u * (2 * SP + s); };
   auto a_empty = [&](int s) { return bar0 + 8u * (2 * SP + SA + s); };
-  auto b_full = [&](int s) { return bar0 + 8u * (2 * SP + 2 * SA + s); };
-  auto b_empty = [&](int s) { return bar0 + 8u * (2 * SP + 2 * SA + SB + s); };
-  constexpr int kX = 2 * SP + 2 * SA + 2 * SB;
+  constexpr int kX = 2 * SP + 2 * SA;
   auto acc_full = [&](int s) { return bar0 + 8u * (kX + s); };
   auto acc_empty = [&](int s) { return bar0 + 8u * (kX + 2 + s); };
   constexpr int MS = C::kMetaSlots;
@@ -292,12 +290,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       mbar_init(pk_empty(s), 4);
     }
     for (int s = 0; s < SA; ++s) {
-      mbar_init(a_full(s), 4);  // one decode group (4 warps)
+      mbar_init(a_full(s), 4 + 1);  // one decode group (4 warps) + the token-tile lane
       mbar_init(a_empty(s), 1);
-    }
-    for (int s = 0; s < SB; ++s) {
-      mbar_init(b_full(s), 1);  // the loading lane (+ transaction bytes)
-      mbar_init(b_empty(s), 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(acc_full(s), C::kIssuers);
@@ -408,25 +402,17 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           mbar_wait(a_full(sa), (gs / SA) & 1, kErrWaitAbFull);
           DSV4_TRACE_EV(3, gs);
           const uint32_t a_tmem = tmem + C::kAColBase + sa * 64;
+          tc_fence_after();
           const int nkb = stage_kb(ks0 + s);
+          const uint64_t bdesc = bdesc0 + static_cast<uint64_t>(((gs % SB) * C::kBBytes) >> 4);
 #pragma unroll
-          for (int h = 0; h < BU; ++h) {
-            const uint32_t u = gs * BU + h;
-            const int sb = u % SB;
-            mbar_wait(b_full(sb), (u / SB) & 1, kErrWaitAbFull);
-            tc_fence_after();
-            const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((sb * C::kUnitBytes) >> 4);
-#pragma unroll
-            for (int kq = 0; kq < 8 / BU; ++kq) {
-              const int kk = h * (8 / BU) + kq;  // 32-K block of the stage
-              if (kk < nkb)
-                mma_i8_ts(d_tmem, a_tmem + kk * 8,
-                          bdesc + static_cast<uint64_t>(((kq >> 2) * C::kBHalf + (kq & 3) * 32) >> 4),
-                          idesc, (s > s_first || kk > 0) ? 1u : 0u);
-            }
-            mma_commit(b_empty(sb));
+          for (int kk = 0; kk < 8; ++kk) {
+            if (kk < nkb)
+              mma_i8_ts(d_tmem, a_tmem + kk * 8,
+                        bdesc + static_cast<uint64_t>(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4),
+                        idesc, (s > s_first || kk > 0) ? 1u : 0u);
           }
-          mma_commit(a_empty(sa));
+          mma_commit(a_empty(sa));  // frees the A slot and (for the loader) the B slot
           DSV4_TRACE_EV(6, gs);
         }
         mma_commit(acc_full(as));
@@ -454,34 +440,23 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           k_range(it, ks0, nks);
           const int row0 = p.moe ? it.b * p.block_m : it.b * TN;
           for (int s = 0; s < nks; ++s, ++g) {
-            if (BU == 2) {
-              // two 128-K units per stage, box {128, TN, 1} each
-#pragma unroll
-              for (int h = 0; h < BU; ++h) {
-                const uint32_t u = g * BU + h;
-                const int sb = u % SB;
-                mbar_wait(b_empty(sb), ((u / SB) & 1) ^ 1, kErrWaitAbEmpty);
-                const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kUnitBytes);
-                mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(C::kUnitBytes));
-                tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2 + h, b_full(sb), pol);
-              }
-              continue;
-            }
             const int sb = g % SB;
-            mbar_wait(b_empty(sb), ((g / SB) & 1) ^ 1, kErrWaitAbEmpty);
+            const uint32_t ready = a_full(g % SA);
+            if (g >= static_cast<uint32_t>(SB))  // B slot free once stage g - SB is done
+              mbar_wait(a_empty((g - SB) % SA), ((g - SB) / SA) & 1, kErrWaitAbEmpty);
             DSV4_TRACE_EV(7, g);
             const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
             if (p.b_mode == 2) {
               // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves
-              mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(C::kBBytes));
-              tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, b_full(sb), pol);
+              mbar_arrive_expect_tx(ready, static_cast<uint32_t>(C::kBBytes));
+              tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ready, pol);
             } else {
               const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
-              mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(nhalf * C::kBHalf));
-              tma_load_2d(b_base, &p.map_act, (ks0 + s) * 256, row0, b_full(sb), pol);
+              mbar_arrive_expect_tx(ready, static_cast<uint32_t>(nhalf * C::kBHalf));
+              tma_load_2d(b_base, &p.map_act, (ks0 + s) * 256, row0, ready, pol);
               if (nhalf == 2)
                 tma_load_2d(b_base + C::kBHalf, &p.map_act, (ks0 + s) * 256 + 128, row0,
-                            b_full(sb), pol);
+                            ready, pol);
             }
             DSV4_TRACE_EV(4, g);
           }
@@ -579,17 +554,18 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           // Warps 2 and 3 take alternate stages and gather only the rows up to
           // the last valid one (4 at a time, lane l -> rows 4l .. 4l+3 of both
           // 128-K halves); the MMA columns beyond are never stored.
-          // (one B unit per stage: 256-token tiles never run in gather4 mode)
           const int last = max(meta_last(ms)[0], meta_last(ms)[1]);
           const int n_rows = ((max(last, 0) + 4) / 4) * 4;
-          for (int s = 0; s < nks && BU == 1; ++s, ++g) {
+          for (int s = 0; s < nks; ++s, ++g) {
             if (static_cast<int>(g & 1) != warp - 2) continue;
             const int sb = g % SB;
+            const uint32_t ready = a_full(g % SA);
             const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
             if (lane == 0) {
-              mbar_wait(b_empty(sb), ((g / SB) & 1) ^ 1, kErrWaitAbEmpty);
+              if (g >= static_cast<uint32_t>(SB))  // B slot free once stage g - SB is done
+                mbar_wait(a_empty((g - SB) % SA), ((g - SB) / SA) & 1, kErrWaitAbEmpty);
               DSV4_TRACE_EV(7, g);
-              mbar_arrive_expect_tx(b_full(sb), static_cast<uint32_t>(nhalf * n_rows * 128));
+              mbar_arrive_expect_tx(ready, static_cast<uint32_t>(nhalf * n_rows * 128));
             }
             __syncwarp();
             const int x0 = (ks0 + s) * 256;
@@ -598,10 +574,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
               const uint32_t dst = b_base + (r >> 3) * 1024 + (r & 7) * 128;
               // padding rows read the out-of-range row -1: zeros
               tma_gather4(dst, &p.map_act, x0, src_s[r], src_s[r + 1], src_s[r + 2],
-                          src_s[r + 3], b_full(sb), pol);
+                          src_s[r + 3], ready, pol);
               if (nhalf == 2)
                 tma_gather4(dst + C::kBHalf, &p.map_act, x0 + 128, src_s[r], src_s[r + 1],
-                            src_s[r + 2], src_s[r + 3], b_full(sb), pol);
+                            src_s[r + 2], src_s[r + 3], ready, pol);
             }
             if (lane == 0) DSV4_TRACE_EV(4, g);
           }
