@@ -141,7 +141,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
 }
 
 // ---------------------------------------------------------------------------
-// Bulk async copies (TMA engine, untiled) and Ampere-style cp.async
+// Bulk async copies (TMA engine, untiled and tiled)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;
@@ -212,21 +212,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(src_bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -261,17 +246,6 @@ __device__ __forceinline__ void tc_fence_before() {
 
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32.
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]^T: A (M=128 lanes x K int8, K-major,
