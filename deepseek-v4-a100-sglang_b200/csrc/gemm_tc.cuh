@@ -39,9 +39,10 @@
 // The per-SM TMA unit spends on the order of 100 cycles on every copy
 // instruction however small, against ~750 cycles per stage at full HBM rate,
 // so the number of copies per stage, not their bytes, is what is budgeted.
-//   warps 4..7   epilogue: TMEM -> registers -> scales -> bf16 / int32 /
-//                SwiGLU -> global
-//   warps 8..    FP4 -> INT8 decode from the packed ring straight into TMEM
+//   warps 4..    epilogue (4 warps, or 8 in two groups for 256-token tiles):
+//                TMEM -> registers -> scales -> bf16 / int32 / SwiGLU ->
+//                shared-memory staging -> 16-byte global stores
+//   then         FP4 -> INT8 decode from the packed ring straight into TMEM
 //                (tcgen05.st), kDecodeGroups groups of 4 warps, group g % G
 //                takes stage g: one 64-column A slot per 128x256 stage
 //   last warps   MMA issuers 1.. (issuer g % kIssuers takes stage g)
