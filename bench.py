@@ -232,19 +232,49 @@ def run_workload(weights, m, zipf, steps, warmup, dev, rank, world, hbm, tops_i8
     hx, hid, htw = x.pin_memory(), ids.pin_memory(), tw.pin_memory()
     hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
     import dsv4_b200 as D
-    for _ in range(2):
-        o = D.mxfp4_int8_moe_forward(hx.to(dev, non_blocking=True), weights,
-                                     hid.to(dev, non_blocking=True), htw.to(dev, non_blocking=True),
-                                     hidden_size=H, intermediate_size=I)
-        hout.copy_(o, non_blocking=True)
+    main = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    bufs = [(torch.empty_like(x, device=dev), torch.empty_like(ids, device=dev),
+             torch.empty_like(tw, device=dev)) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_steps(n):
+        # Serving-style pipeline: step i+1's inputs upload (copy stream `up`)
+        # and step i's output downloads (`down`) while step i computes; every
+        # step still copies its own inputs from pinned host memory and its
+        # output back.  Buffers alternate; events order their reuse.
+        def upload(i):
+            b = bufs[i % 2]
+            with torch.cuda.stream(up):
+                if i >= 2:
+                    up.wait_event(ev_used[i % 2])
+                b[0].copy_(hx, non_blocking=True)
+                b[1].copy_(hid, non_blocking=True)
+                b[2].copy_(htw, non_blocking=True)
+                ev_in[i % 2].record(up)
+
+        up.wait_stream(main)
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            main.wait_event(ev_in[i % 2])
+            b = bufs[i % 2]
+            o = D.mxfp4_int8_moe_forward(b[0], weights, b[1], b[2], hidden_size=H,
+                                         intermediate_size=I)
+            ev_used[i % 2].record(main)
+            down.wait_event(ev_used[i % 2])
+            with torch.cuda.stream(down):
+                hout.copy_(o, non_blocking=True)
+            o.record_stream(down)
+        main.wait_stream(down)
+
+    e2e_steps(2)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(steps):
-        o = D.mxfp4_int8_moe_forward(hx.to(dev, non_blocking=True), weights,
-                                     hid.to(dev, non_blocking=True), htw.to(dev, non_blocking=True),
-                                     hidden_size=H, intermediate_size=I)
-        hout.copy_(o, non_blocking=True)
+    e2e_steps(steps)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / steps
@@ -482,7 +512,9 @@ def main():
                            "w2_gbs": dec["w2_bytes"] / (dec["w2_ms"] * 1e-3) / 1e9},
         "e2e": {"value": total_tokens / (dec["e2e_ms"] * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"],
-                "ms_per_step": dec["e2e_ms"]},
+                "ms_per_step": dec["e2e_ms"],
+                "transfers": "pinned host copies of every step, overlapped with the "
+                             "neighbouring steps' compute (two copy streams)"},
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "clocks": dec["clocks"],
     }
@@ -498,7 +530,9 @@ def main():
                          "peak_source": f"2 x {peak_src} bf16 dense (kind::i8 rate = 2x kind::f16)",
                          "w13_tops": pre["w13_ops"] / (pre["w13_ms"] * 1e-3) / 1e12,
                          "w2_tops": pre["w2_ops"] / (pre["w2_ms"] * 1e-3) / 1e12},
-            "e2e": {"value": PREFILL_M * world / (pre["e2e_ms"] * 1e-3), "unit": "tokens/s"},
+            "e2e": {"value": PREFILL_M * world / (pre["e2e_ms"] * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": pre["h2d"], "d2h_bytes_per_step": pre["d2h"],
+                    "ms_per_step": pre["e2e_ms"]},
         }
     if cpu is not None:
         line["cpu_baseline"] = cpu
