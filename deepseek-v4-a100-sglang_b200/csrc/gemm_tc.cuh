@@ -622,6 +622,13 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       // latency overlaps the chunk's work.
       int32_t pre[16];
       if constexpr (C::kIssuers == 1) tmem_ld_x16(t0 + 16 * eh, pre);
+      bool acc_released = false;
+      auto release_acc = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty(as));
+        acc_released = true;
+      };
       auto load16 = [&](int c0, int32_t (&v)[16]) {
         if (kBiased) {  // row-sum corrections of the 16 tokens, 4 vector loads
 #pragma unroll
@@ -648,6 +655,11 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             for (int q = 0; q < 16; ++q) v[q] += w[q];
           }
         }
+        // One accumulator (no second slot to run ahead into): after this
+        // warp's last chunk load its TMEM reads are complete, so the
+        // accumulator is handed back now and the next item's MMAs overlap
+        // the chunk's scaling and stores.
+        if (C::kIssuers == 1 && c0 + 16 * EH >= n_mma) release_acc();
       };
 
       // bf16((f32(acc) * a_scale) * cs) of the 16 tokens into the staging
@@ -746,13 +758,13 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           }
         }
       }
-      tc_fence_before();
+      if (!acc_released) {  // a group with no chunk of this item
+        if constexpr (C::kIssuers == 1) tmem_ld_wait_regs(pre);
+        release_acc();
+      }
       __syncwarp();
       if (tid == 128) DSV4_TRACE_EV(11, t);
-      if (lane == 0) {
-        mbar_arrive(acc_empty(as));
-        mbar_arrive(meta_empty(ms));
-      }
+      if (lane == 0) mbar_arrive(meta_empty(ms));
       g += nks;
       ++t;
     }
