@@ -6,6 +6,7 @@ import re
 from pathlib import Path
 
 import pytest
+import torch
 
 ROOT = Path(__file__).resolve().parent.parent
 HEADER = ROOT / "include" / "dsv4_b200.h"
@@ -50,3 +51,27 @@ def test_tile_policy():
     assert D.max_mxfp4_int8_moe_block_m(64, 8, 256) == 16
     assert D.max_mxfp4_int8_moe_block_m(8192, 8, 256) == 128
     assert D.select_mxfp4_int8_moe_tile_shape(13, 2, 4)[0] == 16
+
+
+def test_sorted_tile_policy(monkeypatch):
+    import dsv4_b200 as D
+    monkeypatch.delenv("SGLANG_DSV4_MXFP4_INT8_BLOCK_M", raising=False)
+    # decode: the reference policy's small tile is kept
+    assert D.select_sorted_block_m(64, 8, 256) == 16
+    # prefill: 8192 x 8 routes over 256 experts = 256 per expert -> 256-token tiles
+    assert D.select_sorted_block_m(8192, 8, 256) == 256
+    # just below 256 routed tokens per expert: the 128-token tile stays
+    assert D.select_sorted_block_m(8160, 8, 256) == 128
+    # a forced tile is honoured, never widened
+    monkeypatch.setenv("SGLANG_DSV4_MXFP4_INT8_BLOCK_M", "128")
+    assert D.select_sorted_block_m(8192, 8, 256) == 128
+
+
+def test_router_topk_argument_checks():
+    import dsv4_b200 as D
+    with pytest.raises(ValueError, match="2-D"):
+        D.router_topk(torch.zeros(4, dtype=torch.float32), 2)
+    with pytest.raises(ValueError, match="2-D"):
+        D.router_topk(torch.zeros((4, 8), dtype=torch.int32), 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        D.router_topk(torch.zeros((4, 8), dtype=torch.float32), 2)
