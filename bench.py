@@ -61,6 +61,7 @@ class Clocks:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.skip = 0
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"dsv4_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
@@ -76,6 +77,13 @@ class Clocks:
             self.proc = None
         return self
 
+    def mark(self):
+        """Count only samples written from now on (the load window)."""
+        try:
+            self.skip = len(self.path.read_text().splitlines())
+        except Exception:
+            self.skip = 0
+
     def __exit__(self, *a):
         if self.proc is not None:
             self.proc.terminate()
@@ -89,7 +97,7 @@ class Clocks:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
+        for line in self.path.read_text().splitlines()[self.skip:]:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -106,7 +114,8 @@ class Clocks:
         except Exception:
             pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window": "untimed steps of the same load leading into the timed steps, and the timed steps"}
 
 
 def make_weights(dev, seed, experts=None):
@@ -208,6 +217,16 @@ def run_workload(weights, m, zipf, steps, warmup, dev, rank, world, hbm, tops_i8
     clk = Clocks(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else
                  int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[torch.cuda.current_device()]))
     with (clk if sample_clocks else _Null()):
+        if sample_clocks:
+            # ~0.5 s of the same steps leading into the timed ones, so the
+            # 50 ms sampler sees the GPU under this load (the timed steps
+            # alone last a few ms)
+            clk.mark()
+            t0 = time.time()
+            while time.time() - t0 < 0.5:
+                for _ in range(20):
+                    layer(xd, idd, twd)
+                torch.cuda.synchronize()
         start.record()
         for _ in range(steps):
             layer(xd, idd, twd, record=True)
@@ -288,7 +307,7 @@ def run_workload(weights, m, zipf, steps, warmup, dev, rank, world, hbm, tops_i8
     return res
 
 
-def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks):
+def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks, soak_steps=0):
     """Expert-parallel layer: this rank holds E/world experts and m tokens."""
     import torch
     import torch.distributed as dist
@@ -309,6 +328,12 @@ def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks):
     with (clk if sample_clocks else _Null()):
         # the sampler is up before the barrier, so no rank waits on another's start-up
         dist.barrier()
+        if sample_clocks:
+            clk.mark()
+        # the same number of untimed steps on every rank (collectives stay
+        # matched), so the sampler sees the GPU under this load
+        for _ in range(soak_steps):
+            layer.forward(xd, idd, twd)
         torch.cuda.synchronize()
         start.record()
         for _ in range(steps):
@@ -544,7 +569,8 @@ def main():
 
 def main_ep(args, dev, rank, world, hbm):
     import torch.distributed as dist
-    dec = run_ep(DECODE_M, None, args.steps, args.warmup, dev, rank, world, sample_clocks=(rank == 0))
+    dec = run_ep(DECODE_M, None, args.steps, args.warmup, dev, rank, world, sample_clocks=(rank == 0),
+                 soak_steps=300)
     pre = None
     if not args.no_prefill:
         pre = run_ep(EP_PREFILL_TOKENS // world, 1.1, max(3, args.steps // 20), args.warmup, dev, rank,
