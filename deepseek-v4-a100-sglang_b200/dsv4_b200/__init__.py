@@ -32,3 +32,4 @@ from .jit_ops import (  # noqa: F401
     prewarm_mxfp4_int8_dense_jit_module,
     prewarm_mxfp4_int8_moe_jit_modules,
 )
+from ._native import DeviceTimeoutError, check_device_status  # noqa: F401,E402

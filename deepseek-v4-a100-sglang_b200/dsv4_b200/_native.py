@@ -113,6 +113,19 @@ def device_status(reset: bool = False) -> int:
     return v.value
 
 
+def check_device_status() -> int:
+    """Read (and clear) the device status word; raise DeviceTimeoutError if a
+    kernel gave up a bounded wait since the last check (its outputs are then
+    garbage).  Synchronises with the device: call it at a sync point, e.g.
+    after a step, not inside a captured graph."""
+    code = device_status(reset=True)
+    if code != 0:
+        raise DeviceTimeoutError(
+            f"a kernel abandoned a bounded wait (device status 0x{code:x}); "
+            "results since the last check are invalid")
+    return 0
+
+
 def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 

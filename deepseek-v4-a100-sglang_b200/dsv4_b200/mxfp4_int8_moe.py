@@ -186,18 +186,6 @@ def max_mxfp4_int8_moe_block_m(m: int, topk: int, experts: int) -> int:
     return min(_MAX_BLOCK_M, max(16, 1 << (avg - 1).bit_length()))
 
 
-def _parse_tile_shape(text: str) -> tuple[int, int]:
-    parts = text.strip().lower().replace("x", ",").split(",")
-    if len(parts) != 2:
-        raise ValueError(f"invalid tile shape {text!r}, expected MxN")
-    block_m, block_n = int(parts[0]), int(parts[1])
-    if block_m not in _VALID_BLOCK_M:
-        raise ValueError("block_m must be 16, 32, 64, or 128")
-    if block_n not in _VALID_BLOCK_N:
-        raise ValueError("block_n must be 32, 64, or 128")
-    return block_m, block_n
-
-
 def _select_moe_tile_shape(m: int, topk: int, experts: int) -> tuple[int, int]:
     """B200 tile policy with the reference's env overrides and cap
     (PYMOE:816-839).  The token tile equals block_m and one decoded weight
@@ -291,15 +279,6 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
 
 
 _moe_align_block_size = moe_align_block_size
-
-
-def _apply_swiglu(x: torch.Tensor, clamp_limit: float | None) -> torch.Tensor:
-    """PYMOE:872-877 (kept for callers of the unfused path)."""
-    gate, up = x.chunk(2, dim=-1)
-    if clamp_limit is not None:
-        gate = gate.clamp(max=clamp_limit)
-        up = up.clamp(min=-clamp_limit, max=clamp_limit)
-    return torch.nn.functional.silu(gate) * up
 
 
 def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWeights,

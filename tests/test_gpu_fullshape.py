@@ -1,0 +1,202 @@
+"""GPU parity at the benchmarked production shapes.
+
+Every stage of the layer that bench.py times is checked at its full size
+against the torch checker (tests/torch_checker.py, itself pinned bit for bit to
+the numpy oracle by tests/test_torch_checker.py), each stage fed the CUDA
+path's own previous output so one stage's allowed SwiGLU difference cannot
+hide another's error:
+
+* decode  H=7168, I=2048, E=256, top-8 sigmoid+bias, M=64 (16-token tiles),
+  and the same with uniform routing (most experts touched);
+* prefill M=8192 with Zipf(1.1) skew (256-token tiles, one expert above
+  1,000 tokens), and M=8192 with uniform routing;
+* dense   BASELINE configs[1]: M in {1, 16, 128, 4096}, K=7168, N=4096.
+
+Tolerances (written here, as in test_gpu_parity.py): align, quant, sorted
+rows, int32 accumulators, the bf16 GEMM epilogues and the combine are
+bit-exact; the fused SwiGLU may differ by 1 bf16 ulp on at most 0.5 % of
+elements.  A token subset of the decode layer is compared with the
+reference's float MoE at the reference's threshold (rel-L2 < 0.08).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mxfp4_int8_oracle as O
+import gen_inputs as G
+import torch_checker as TC
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    import dsv4_b200 as D
+    import dsv4_b200.jit_ops as J
+
+DEV = "cuda"
+H, I, E, TOPK = 7168, 2048, 256, 8
+
+
+def _u16(t):
+    return t.view(torch.int16).to(torch.int32) & 0xFFFF
+
+
+def _swiglu_ok(got, ref):
+    d = (_u16(got) - _u16(ref)).abs()
+    assert int(d.max()) <= 1, f"SwiGLU differs by {int(d.max())} ulp"
+    assert float((d > 0).float().mean()) <= 0.005
+
+
+@pytest.fixture(scope="module")
+def weights():
+    """Raw MXFP4 (kept for the float reference) and the repacked layer."""
+    g = torch.Generator(device=DEV)
+    g.manual_seed(42)
+    raw, rep = [], []
+    for n, k in ((2 * I, H), (H, I)):
+        w = torch.randint(0, 256, (E, n, k // 2), device=DEV, dtype=torch.uint8, generator=g)
+        s = torch.randint(119, 124, (E, n, k // 32), device=DEV, dtype=torch.uint8, generator=g)
+        raw.append((w, s))
+        rep.extend(D.remap_mxfp4_weight_for_int8(w, s))
+    torch.cuda.synchronize()
+    return raw, D.Mxfp4Int8MoeWeights(*rep, 3)
+
+
+def _routing(m, seed, kind):
+    if kind == "uniform":
+        gen = torch.Generator()
+        gen.manual_seed(seed)
+        logits = torch.randn(m, E, generator=gen)
+        scores = torch.sigmoid(logits)
+        _, ids = torch.topk(scores, TOPK, dim=-1)
+        w = torch.gather(scores, 1, ids)
+        return ids.to(torch.int32), (w / w.sum(-1, keepdim=True)).float()
+    return G.routing_sigmoid_bias_topk(m, E, TOPK, seed, zipf_s=1.1 if kind == "zipf" else None)
+
+
+def _run_layer_stages(weights, m, kind, seed):
+    raw, w = weights
+    ids, tw = _routing(m, seed, kind)
+    x = G.randn_bf16((m, H), seed + 1)
+    xd, idd, twd = x.to(DEV), ids.to(DEV), tw.to(DEV)
+    nv = m * TOPK
+    bm = D.select_sorted_block_m(m, TOPK, E)
+    kw = dict(hidden_size=H, intermediate_size=I, topk=TOPK, block_m=bm, num_valid_tokens=nv)
+
+    # align: bit-exact vs the numpy oracle
+    s, e, n = D.moe_align_block_size(idd, bm, E)
+    os_, oe, ontp, _ = O.moe_align_block_size(ids.numpy(), bm, E)
+    assert int(n.item()) == int(ontp[0])
+    np.testing.assert_array_equal(s.cpu().numpy(), os_)
+    np.testing.assert_array_equal(e.cpu().numpy(), oe)
+    cap = s.numel()
+    n_pad = int(n.item())
+    sl = s.long()
+    valid = (torch.arange(cap, device=DEV) < n_pad) & (sl >= 0) & (sl < nv)
+    slots = sl[valid]
+
+    # quant
+    q, qs = D.quantize_per_token_int8(xd)
+    rq, rqs = TC.quantize_rows(xd)
+    assert torch.equal(q, rq) and torch.equal(qs, rqs)
+
+    # sorted rows
+    a13, s13, r13 = J.moe_sort_rows(q, qs, s, n, topk=TOPK, num_valid_tokens=nv)
+    rows13 = a13.view(H // 128, cap, 128).permute(1, 0, 2).reshape(cap, H)
+    assert torch.equal(rows13[valid], q[slots // TOPK])
+    assert torch.equal(s13[valid], qs[slots // TOPK])
+    assert torch.equal(r13[valid].long(), q[slots // TOPK].long().sum(1))
+
+    # W13 + SwiGLU (rows by sorted position)
+    inter = torch.zeros((cap, I), dtype=torch.bfloat16, device=DEV)
+    J.mxfp4_int8_moe_gemm_swiglu_sorted(a13, s13, r13, w.w13_mxfp4, w.w13_shift2,
+                                        w.w13_channel_scale, inter, s, e, n, **kw)
+    gu, written = TC.moe_gemm_bf16(rows13, s13, w.w13_mxfp4, w.w13_shift2, w.w13_channel_scale,
+                                   s, e, n, block_m=bm, topk=TOPK, num_valid=nv,
+                                   source_rows_are_slots=False, by_position=True)
+    assert torch.equal(written, valid)
+    _swiglu_ok(inter[valid], TC.swiglu_bf16(gu[valid], I))
+
+    # requant of the CUDA intermediate
+    a2, s2, r2 = J.quantize_sorted_int8(inter, s, n, num_valid_tokens=nv)
+    rows2 = a2.view(I // 128, cap, 128).permute(1, 0, 2).reshape(cap, I)
+    rq2, rqs2 = TC.quantize_rows(inter[valid])
+    assert torch.equal(rows2[valid], rq2) and torch.equal(s2[valid], rqs2)
+    assert torch.equal(r2[valid].long(), rq2.long().sum(1))
+
+    # W2 -> routed rows by slot
+    routed = torch.empty((nv, H), dtype=torch.bfloat16, device=DEV)
+    J.mxfp4_int8_moe_gemm_sorted(a2, s2, r2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale, routed,
+                                 s, e, n, **kw)
+    ref_pos, _ = TC.moe_gemm_bf16(rows2, s2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale, s, e, n,
+                                  block_m=bm, topk=TOPK, num_valid=nv, source_rows_are_slots=True,
+                                  by_position=True)
+    assert torch.equal(routed[slots], ref_pos[valid])
+
+    # combine with routed scaling
+    out = torch.empty((m, H), dtype=torch.bfloat16, device=DEV)
+    J.mxfp4_int8_moe_reduce(routed, twd, out, hidden_size=H, intermediate_size=I, topk=TOPK,
+                            block_m=min(bm, 128), num_valid_tokens=nv, routed_scaling_factor=2.5)
+    assert torch.equal(out, TC.moe_reduce_bf16(routed, twd, m, TOPK, nv, 2.5))
+
+    # the public forward runs the same kernels: identical output
+    fwd = D.mxfp4_int8_moe_forward(xd, w, idd, twd, hidden_size=H, intermediate_size=I,
+                                   routed_scaling_factor=2.5)
+    assert torch.equal(fwd, out)
+    assert D.check_device_status() == 0
+    counts = torch.bincount(ids.reshape(-1).long(), minlength=E)
+    return dict(x=x, ids=ids, tw=tw, out=fwd, bm=bm, counts=counts)
+
+
+def test_decode_layer_full_shape_bias(weights):
+    r = _run_layer_stages(weights, 64, "bias", 1000)
+    assert r["bm"] == 16
+    # token subset against the reference's float MoE (TEST_MOE:165-258 threshold)
+    raw, _ = weights
+    sub = slice(0, 2)
+    sub_ids = r["ids"][sub]
+    experts = torch.unique(sub_ids).tolist()
+    remap = {ex: j for j, ex in enumerate(experts)}
+    local = sub_ids.clone().apply_(lambda v: remap[v])
+    pick = torch.tensor(experts, device=DEV)
+    (w13, s13), (w2, s2) = raw
+    ref = O.mxfp4_moe_reference_torch(r["x"][sub], w13[pick].cpu(), s13[pick].cpu(),
+                                      w2[pick].cpu(), s2[pick].cpu(), local, r["tw"][sub])
+    got = r["out"][sub].float().cpu() / 2.5
+    assert O.relative_l2(got.numpy(), ref.float().numpy()) < 0.08
+
+
+def test_decode_layer_full_shape_uniform(weights):
+    r = _run_layer_stages(weights, 64, "uniform", 1100)
+    assert int((r["counts"] > 0).sum()) > 200
+
+
+def test_prefill_layer_full_shape_zipf(weights):
+    r = _run_layer_stages(weights, 8192, "zipf", 1200)
+    assert r["bm"] == 256
+    assert int(r["counts"].max()) > 1000
+
+
+def test_prefill_layer_full_shape_uniform(weights):
+    r = _run_layer_stages(weights, 8192, "uniform", 1300)
+    assert r["bm"] == 256
+    assert int((r["counts"] > 0).sum()) == E
+
+
+@pytest.mark.parametrize("m", [1, 16, 128, 4096])
+def test_dense_config1_full_shape(m):
+    n, k = 4096, 7168
+    g = torch.Generator(device=DEV)
+    g.manual_seed(7 + m)
+    w = torch.randint(0, 256, (n, k // 2), device=DEV, dtype=torch.uint8, generator=g)
+    sc = torch.randint(119, 124, (n, k // 32), device=DEV, dtype=torch.uint8, generator=g)
+    wt = D.prepare_mxfp4_int8_dense_weight(w, sc)
+    x = G.randn_bf16((m, k), 9 + m).to(DEV)
+    q, qs = D.quantize_per_token_int8(x)
+    acc = J.mxfp4_int8_dense_gemm_i32(q, wt.weight_mxfp4, wt.weight_shift2, n)
+    assert torch.equal(acc.long(), TC.dense_gemm_i32(q, wt.weight_mxfp4, wt.weight_shift2, n))
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
+    J.mxfp4_int8_dense_gemm(q, qs, wt.weight_mxfp4, wt.weight_shift2, wt.weight_channel_scale, out)
+    assert torch.equal(out, TC.dense_gemm_bf16(q, qs, wt.weight_mxfp4, wt.weight_shift2, wt.weight_channel_scale))
+    assert torch.equal(D.mxfp4_int8_dense_forward(x, wt), out)
+    assert D.check_device_status() == 0
