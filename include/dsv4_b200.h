@@ -279,7 +279,9 @@ DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm_i32(const int8_t* a_q, int64_t m, i
  * before any stream capture.  The array is shared by every call in the
  * process: calls that overlap on the GPU (other streams, other threads)
  * race on it; serialise them.  Nothing in it needs to start at zero (every
- * call overwrites the words it reads). */
+ * call overwrites the words it reads).  The looked-up address is cached for
+ * the life of the process: do not keep using the library on a device after
+ * cudaDeviceReset (the cached address would be stale). */
 DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm_noalloc(const int8_t* a_q, const float* a_scale,
                                                      int64_t m, int64_t k, const uint8_t* b_mxfp4,
                                                      const uint8_t* b_shift2, int64_t shift_stride,

@@ -29,7 +29,8 @@ def _case(m, n, k, seed):
     return q, qs, b[0], sh[0], cs[0]
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 4096, 1024), (16, 256, 1024), (128, 512, 512)])
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 1024), (16, 256, 1024), (128, 512, 512),
+                                   (128, 4096, 7168)])  # the last: the largest size the array holds
 def test_noalloc_matches_allocating_entry_twice(m, n, k):
     from dsv4_b200 import _native as N
     q, qs, b, sh, cs = _case(m, n, k, 500 + m)
@@ -56,4 +57,15 @@ def test_noalloc_rejects_sizes_beyond_the_workspace():
     with pytest.raises(RuntimeError, match="fixed split-K workspace"):
         N.call("dsv4_b200_mxfp4_int8_dense_gemm_noalloc", q.data_ptr(), qs.data_ptr(), 129, 256,
                b.data_ptr(), sh.data_ptr(), sh.shape[0], cs.data_ptr(), 256, out.data_ptr(),
+               torch.cuda.current_stream().cuda_stream)
+
+
+def test_noalloc_rejects_n_beyond_the_workspace_at_m_128():
+    """m = 128 with n = 4224: 4 * 128 * 4224 words exceed the 8 MiB array."""
+    from dsv4_b200 import _native as N
+    q, qs, b, sh, cs = _case(128, 4224, 256, 8)
+    out = torch.empty((128, 4224), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="fixed split-K workspace"):
+        N.call("dsv4_b200_mxfp4_int8_dense_gemm_noalloc", q.data_ptr(), qs.data_ptr(), 128, 256,
+               b.data_ptr(), sh.data_ptr(), sh.shape[0], cs.data_ptr(), 4224, out.data_ptr(),
                torch.cuda.current_stream().cuda_stream)
