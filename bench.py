@@ -36,6 +36,11 @@ H, I, E, TOPK = 7168, 2048, 256, 8
 DECODE_M, PREFILL_M = 64, 8192
 EP_PREFILL_TOKENS = 32768  # global batch split evenly across ranks
 EXP_RANGE = (-8, -4)
+# DRAM bytes (read + write) per algorithmic byte of the decode W13 GEMM,
+# measured by an ncu capture of that kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum); scales this launch's algorithmic bytes into the
+# roofline's `traffic`.
+TRAFFIC_RATIO_W13_DECODE = 1.015
 
 
 def _set_experts(e):
@@ -195,15 +200,23 @@ class Layer:
 LAUNCHES_PER_STEP = 7  # align, quant, sort rows, W13+SwiGLU, quant, W2, combine
 
 
-def routing(m, seed, zipf):
+MODEL_SEED = 7  # router bias and expert popularity: properties of the model, shared by all ranks
+
+
+def routing(m, seed, kind):
+    """kind: "bias" (sigmoid + per-expert bias), "zipf"
+    (the same plus Zipf(1.1) expert popularity, configs[3]) or "uniform"."""
     import gen_inputs as G
-    return G.routing_sigmoid_bias_topk(m, E, TOPK, seed, zipf_s=zipf)
+    if kind == "uniform":
+        return G.routing_uniform_topk(m, E, TOPK, seed)
+    return G.routing_sigmoid_bias_topk(m, E, TOPK, seed, zipf_s=1.1 if kind == "zipf" else None,
+                                       model_seed=MODEL_SEED)
 
 
-def run_workload(weights, m, zipf, steps, warmup, dev, rank, world, hbm, tops_i8, sample_clocks):
+def run_workload(weights, m, kind, steps, warmup, dev, rank, world, hbm, tops_i8, sample_clocks):
     import torch
     import torch.distributed as dist
-    ids, tw = routing(m, 1000 + rank, zipf)
+    ids, tw = routing(m, 1000 + rank, kind)
     import gen_inputs as G
     x = G.randn_bf16((m, H), 2000 + rank)
     xd, idd, twd = x.to(dev), ids.to(dev), tw.to(dev)
@@ -307,8 +320,11 @@ def run_workload(weights, m, zipf, steps, warmup, dev, rank, world, hbm, tops_i8
     return res
 
 
-def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks, soak_steps=0):
-    """Expert-parallel layer: this rank holds E/world experts and m tokens."""
+def run_ep(m, kind, steps, warmup, dev, rank, world, soak_steps=0):
+    """Expert-parallel layer: this rank holds E/world experts and m tokens.
+    Fixed-capacity exchange (capacity = m on every rank): no host
+    synchronisation inside a step.  Phases are timed with CUDA events in a
+    separate pass so the timed steps carry no extra events."""
     import torch
     import torch.distributed as dist
     import gen_inputs as G
@@ -316,8 +332,8 @@ def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks, soak_steps=0
     e_loc = E // world
     weights = make_weights(dev, 42 + rank, e_loc)
     layer = ExpertParallelMoE(GpuOps(weights, H, I), num_experts=E, hidden_size=H,
-                              capacity_tokens=m if m <= 256 else None)
-    ids, tw = routing(m, 1000 + rank, zipf)
+                              capacity_tokens=m)
+    ids, tw = routing(m, 1000 + rank, kind)
     x = G.randn_bf16((m, H), 2000 + rank)
     xd, idd, twd = x.to(dev), ids.to(dev), tw.to(dev)
     for _ in range(warmup):
@@ -325,11 +341,10 @@ def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks, soak_steps=0
     torch.cuda.synchronize()
     clk = Clocks(local_gpu_index())
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with (clk if sample_clocks else _Null()):
+    with clk:
         # the sampler is up before the barrier, so no rank waits on another's start-up
         dist.barrier()
-        if sample_clocks:
-            clk.mark()
+        clk.mark()
         # the same number of untimed steps on every rank (collectives stay
         # matched), so the sampler sees the GPU under this load
         for _ in range(soak_steps):
@@ -345,6 +360,21 @@ def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks, soak_steps=0
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     stats = dict(layer.last_stats)
+    # per-phase times (max over ranks of each phase's mean)
+    layer.timing = True
+    for _ in range(min(steps, 20)):
+        layer.forward(xd, idd, twd)
+    ph = layer.phase_ms()
+    layer.timing = False
+    pt = torch.tensor([ph[k] for k in layer.PHASES], device=dev)
+    dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+    phases = dict(zip(layer.PHASES, pt.tolist()))
+    # experts this rank touched: the routed ids of every rank that fall in its range
+    all_ids = [torch.empty_like(idd) for _ in range(world)]
+    dist.all_gather(all_ids, idd)
+    mine = torch.cat(all_ids).reshape(-1).long()
+    mine = mine[(mine >= rank * e_loc) & (mine < (rank + 1) * e_loc)]
+    touched = int(torch.unique(mine).numel())
     # end to end: pinned host buffers in, host output back, every step
     hx, hid, htw = x.pin_memory(), ids.pin_memory(), tw.pin_memory()
     hout = torch.empty((m, H), dtype=torch.bfloat16).pin_memory()
@@ -360,9 +390,12 @@ def run_ep(m, zipf, steps, warmup, dev, rank, world, sample_clocks, soak_steps=0
     t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     b13, b2 = weight_bytes_per_expert()
+    tt = torch.tensor([touched], device=dev, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MIN)
     return {"ms": ms, "e2e_ms": float(t.item()), "stats": stats, "e_loc": e_loc,
-            "weight_bytes_local": e_loc * (b13 + b2), "h2d": m * H * 2 + m * TOPK * 8,
-            "d2h": m * H * 2, "clocks": clk.summary() if sample_clocks else None}
+            "phases_ms": phases, "touched_rank0": touched, "touched_min": int(tt.item()),
+            "weight_bytes_touched": touched * (b13 + b2), "h2d": m * H * 2 + m * TOPK * 8,
+            "d2h": m * H * 2, "clocks": clk.summary()}
 
 
 def local_gpu_index():
@@ -396,7 +429,7 @@ def cpu_reference_sample(steps, warmup, tokens_per_step=1):
     from oracle import mxfp4_int8_oracle as O
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    ids, tw = routing(DECODE_M, 1000, None)
+    ids, tw = routing(DECODE_M, 1000, "bias")
     x = G.randn_bf16((DECODE_M, H), 2000)
     times = []
     for step in range(warmup + steps):
@@ -417,6 +450,101 @@ def cpu_reference_sample(steps, warmup, tokens_per_step=1):
     return tokens_per_step / sec, threads, sec
 
 
+DENSE_N, DENSE_K = 4096, 7168
+DENSE_MS = (1, 16, 128, 4096)
+
+
+def run_dense(dev, steps, warmup, hbm, tops_i8):
+    """bf16 A [M, 7168] quantised per token, times an
+    MXFP4 7168 -> 4096 weight.  The weight (14.7 MB) fits in L2, so L2 is
+    flushed before every timed launch; each launch is timed alone with CUDA
+    events on its stream."""
+    import torch
+    import dsv4_b200 as D
+    import dsv4_b200.jit_ops as J
+    import gen_inputs as G
+    n, k = DENSE_N, DENSE_K
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    w = torch.randint(0, 256, (n, k // 2), device=dev, dtype=torch.uint8, generator=g)
+    sc = torch.randint(127 + EXP_RANGE[0], 127 + EXP_RANGE[1] + 1, (n, k // 32), device=dev,
+                       dtype=torch.uint8, generator=g)
+    wt = D.prepare_mxfp4_int8_dense_weight(w, sc)
+    del w, sc
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+
+    def flush():
+        # write a buffer larger than L2, then read another one, so the timed
+        # launch starts with an L2 holding clean, unrelated lines (a dirty L2
+        # would make it pay for 126 MB of write-backs)
+        flush_w.zero_()
+        flush_r.sum()
+
+    wbytes = n * k // 2 + (k // 32 + 3) // 4 * n + 4 * n
+    res = {}
+    clk = Clocks(local_gpu_index())
+    with clk:
+        clk.mark()
+        for m in DENSE_MS:
+            x = G.randn_bf16((m, k), 30 + m)
+            xd = x.to(dev)
+            q, qs = D.quantize_per_token_int8(xd)
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            ld = (n + 31) // 32 * 32
+            part = torch.empty((4, m, ld), dtype=torch.int32, device=dev) if m <= 128 else None
+
+            def gemm():
+                J.mxfp4_int8_dense_gemm(q, qs, wt.weight_mxfp4, wt.weight_shift2,
+                                        wt.weight_channel_scale, out, part)
+
+            for _ in range(warmup):
+                gemm()
+            evs = []
+            for _ in range(steps):
+                flush()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                gemm()
+                b.record()
+                evs.append((a, b))
+            torch.cuda.synchronize()
+            ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+            # end to end through the public op: pinned host x in, host out back
+            hx = x.pin_memory()
+            hout = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+            ee = []
+            for i in range(steps + warmup):
+                flush()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                xd.copy_(hx, non_blocking=True)
+                o = D.mxfp4_int8_dense_forward(xd, wt)
+                hout.copy_(o, non_blocking=True)
+                b.record()
+                if i >= warmup:
+                    ee.append((a, b))
+            torch.cuda.synchronize()
+            e2e_ms = statistics.mean(a.elapsed_time(b) for a, b in ee)
+            alg = wbytes + m * k + 4 * m + m * n * 2
+            ops = 2 * m * n * k
+            gbs = alg / (ms * 1e-3) / 1e9
+            tops = ops / (ms * 1e-3) / 1e12
+            bound = "hbm" if m <= 128 else "tensor"
+            res[str(m)] = {
+                "kernel_ms": ms, "tokens_per_s": m / (ms * 1e-3),
+                "algorithmic_bytes": alg, "gbs": gbs, "hbm_frac": gbs / hbm,
+                "tops": tops, "int8_frac": tops / tops_i8, "bound": bound,
+                "launches": 2 if m <= 128 else 1,
+                "e2e": {"ms": e2e_ms, "tokens_per_s": m / (e2e_ms * 1e-3),
+                        "h2d_bytes": m * k * 2, "d2h_bytes": m * n * 2}}
+    return {"workload": "dense MXFP4/INT8 GEMM (BASELINE configs[1]): bf16 A [M, 7168] "
+                        "quantised per token x MXFP4 7168->4096, bf16 out",
+            "l2": "flushed before every timed launch: a 256 MB write, then a 256 MB read of "
+                  "another buffer (L2 left clean)",
+            "per_m": res, "clocks": clk.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -427,7 +555,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--experts", type=int, default=E,
                     help="number of experts (smaller for ncu captures that must stay a few GB)")
-    ap.add_argument("--only", choices=["decode", "prefill"], default=None,
+    ap.add_argument("--no-dense", action="store_true")
+    ap.add_argument("--only", choices=["decode", "prefill", "decode_uniform", "prefill_uniform"],
+                    default=None,
                     help="run one workload only (profiling); prints its JSON line")
     args = ap.parse_args()
     if args.experts != E:
@@ -481,33 +611,41 @@ def main():
         return
     weights = make_weights(dev, 42)
     if args.only is not None:
-        m, z = (DECODE_M, None) if args.only == "decode" else (PREFILL_M, 1.1)
-        r = run_workload(weights, m, z, args.steps, args.warmup, dev, rank, world, hbm, tops_i8,
+        m, kind = {"decode": (DECODE_M, "bias"), "prefill": (PREFILL_M, "zipf"),
+                   "decode_uniform": (DECODE_M, "uniform"),
+                   "prefill_uniform": (PREFILL_M, "uniform")}[args.only]
+        r = run_workload(weights, m, kind, args.steps, args.warmup, dev, rank, world, hbm, tops_i8,
                          sample_clocks=False)
-        if rank == 0:
-            r.pop("clocks", None)
-            print(json.dumps({"only": args.only, "experts": E, **r}))
+        r.pop("clocks", None)
+        print(json.dumps({"only": args.only, "experts": E, **r}))
         return
-    dec = run_workload(weights, DECODE_M, None, args.steps, args.warmup, dev, rank, world, hbm,
-                       tops_i8, sample_clocks=True)
-    pre = None
+    legs = {"decode": run_workload(weights, DECODE_M, "bias", args.steps, args.warmup, dev, rank,
+                                   world, hbm, tops_i8, sample_clocks=True)}
     if not args.no_prefill:
-        pre = run_workload(weights, PREFILL_M, 1.1, max(3, args.steps // 10), args.warmup, dev,
-                           rank, world, hbm, tops_i8, sample_clocks=False)
+        legs["decode_uniform"] = run_workload(weights, DECODE_M, "uniform", args.steps, args.warmup,
+                                              dev, rank, world, hbm, tops_i8, sample_clocks=True)
+        psteps = max(3, args.steps // 10)
+        for name, kind in (("prefill", "zipf"), ("prefill_uniform", "uniform")):
+            legs[name] = run_workload(weights, PREFILL_M, kind, psteps, args.warmup, dev, rank,
+                                      world, hbm, tops_i8, sample_clocks=True)
+    del weights
+    torch.cuda.empty_cache()
+    dense = None if args.no_dense else run_dense(dev, max(3, args.steps // 10), args.warmup, hbm,
+                                                 tops_i8)
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if not args.no_cpu_baseline:
         tps, threads, sec = cpu_reference_sample(3, 1)
         cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": "1 token of the M=64 decode batch per step (3 steps, median): dequantise its 8 "
                          "experts to fp32 + per-route SwiGLU MLP, the reference's torch CPU MoE restated"}
-    if rank != 0:
-        return
+    torch.cuda.synchronize()
+    dev_status = D.check_device_status()  # raises if a kernel abandoned a wait
 
-    total_tokens = DECODE_M * world
+    dec = legs["decode"]
     w13_gbs = dec["w13_bytes"] / (dec["w13_ms"] * 1e-3) / 1e9
     line = {
         "metric": "MoE layer tokens/s (decode M=64)",
-        "value": total_tokens / (dec["ms"] * 1e-3),
+        "value": DECODE_M / (dec["ms"] * 1e-3),
         "unit": "tokens/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -520,63 +658,87 @@ def main():
         "data": "synthetic",
         "config": {"workload": "decode MoE layer (BASELINE configs[2]): H=7168 I=2048 E=256 top-8 "
                                "sigmoid+bias routing, M=64 tokens/GPU, MXFP4 weights exps U[-8,-4]",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "block_m": dec["bm"], "l2": "not flushed: 5.7 GB of weights streamed per step",
+                   "parallelism": "single GPU", "block_m": dec["bm"],
+                   "l2": "not flushed: 5.7 GB of weights streamed per step (inputs larger than L2)",
                    "experts_touched": dec["touched"]},
         "roofline": {"bound": "hbm", "kernel": "W13 grouped GEMM + fused SwiGLU",
                      "achieved": w13_gbs, "peak": hbm, "unit": "GB/s", "frac": w13_gbs / hbm,
-                     # DRAM bytes per launch: the 32-expert ncu capture read+wrote 1.015x its
-                     # algorithmic bytes (profiles/moe_decode_w13_gemm_ncu.md); scaled to this launch
-                     "traffic": dec["w13_bytes"] * 1.015, "peak_source": peak_src,
-                     "algorithmic_bytes_per_launch": dec["w13_bytes"],
+                     "traffic": dec["w13_bytes"] * TRAFFIC_RATIO_W13_DECODE,
+                     "traffic_source": "DRAM read+write bytes per algorithmic byte from an ncu "
+                                       "capture of this kernel, times this launch's bytes",
+                     "peak_source": peak_src, "algorithmic_bytes_per_launch": dec["w13_bytes"],
                      "launch_ms": dec["w13_ms"]},
-        "layer_roofline": {"bound": "hbm", "bytes_per_step": dec["layer_bytes"],
-                           "achieved": dec["layer_bytes"] / (dec["ms"] * 1e-3) / 1e9,
-                           "frac": dec["layer_bytes"] / (dec["ms"] * 1e-3) / 1e9 / hbm,
-                           "w2_gemm_ms": dec["w2_ms"],
-                           "w2_gbs": dec["w2_bytes"] / (dec["w2_ms"] * 1e-3) / 1e9},
-        "e2e": {"value": total_tokens / (dec["e2e_ms"] * 1e-3), "unit": "tokens/s",
+        "layer_roofline": _layer_roofline(dec, hbm),
+        "e2e": {"value": DECODE_M / (dec["e2e_ms"] * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"],
                 "ms_per_step": dec["e2e_ms"],
                 "transfers": "pinned host copies of every step, overlapped with the "
                              "neighbouring steps' compute (two copy streams)"},
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "clocks": dec["clocks"],
+        "device_status": dev_status,
     }
-    if pre is not None:
+    if "decode_uniform" in legs:
+        du = legs["decode_uniform"]
+        line["decode_uniform"] = {
+            "workload": "decode layer, uniform routing (no bias): M=64",
+            "value": DECODE_M / (du["ms"] * 1e-3), "unit": "tokens/s", "ms_per_step": du["ms"],
+            "experts_touched": du["touched"], "block_m": du["bm"],
+            "layer_roofline": _layer_roofline(du, hbm),
+            "w13_gbs": du["w13_bytes"] / (du["w13_ms"] * 1e-3) / 1e9,
+            "w13_frac": du["w13_bytes"] / (du["w13_ms"] * 1e-3) / 1e9 / hbm,
+            "e2e": {"value": DECODE_M / (du["e2e_ms"] * 1e-3), "unit": "tokens/s",
+                    "ms_per_step": du["e2e_ms"]},
+            "clocks": du["clocks"]}
+    for name, label in (("prefill", "prefill MoE layer (BASELINE configs[3]): M=8192, Zipf(1.1) "
+                                    "expert skew"),
+                        ("prefill_uniform", "prefill MoE layer, uniform routing: M=8192")):
+        if name not in legs:
+            continue
+        pre = legs[name]
         ops = pre["w13_ops"] + pre["w2_ops"]
-        line["prefill"] = {
-            "workload": "prefill MoE layer (BASELINE configs[3]): M=8192, Zipf(1.1) expert skew",
-            "value": PREFILL_M * world / (pre["ms"] * 1e-3), "unit": "tokens/s",
-            "ms_per_step": pre["ms"], "block_m": pre["bm"],
+        line[name] = {
+            "workload": label,
+            "value": PREFILL_M / (pre["ms"] * 1e-3), "unit": "tokens/s",
+            "ms_per_step": pre["ms"], "block_m": pre["bm"], "experts_touched": pre["touched"],
             "roofline": {"bound": "tensor", "achieved": ops / (pre["ms"] * 1e-3) / 1e12,
                          "peak": tops_i8, "unit": "TOP/s (int8)",
                          "frac": ops / (pre["ms"] * 1e-3) / 1e12 / tops_i8,
                          "peak_source": f"2 x {peak_src} bf16 dense (kind::i8 rate = 2x kind::f16)",
                          "w13_tops": pre["w13_ops"] / (pre["w13_ms"] * 1e-3) / 1e12,
-                         "w2_tops": pre["w2_ops"] / (pre["w2_ms"] * 1e-3) / 1e12},
-            "e2e": {"value": PREFILL_M * world / (pre["e2e_ms"] * 1e-3), "unit": "tokens/s",
+                         "w2_tops": pre["w2_ops"] / (pre["w2_ms"] * 1e-3) / 1e12,
+                         "w13_ms": pre["w13_ms"], "w2_ms": pre["w2_ms"]},
+            "e2e": {"value": PREFILL_M / (pre["e2e_ms"] * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": pre["h2d"], "d2h_bytes_per_step": pre["d2h"],
                     "ms_per_step": pre["e2e_ms"]},
-        }
+            "clocks": pre["clocks"]}
+    if dense is not None:
+        line["dense"] = dense
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+
+
+def _layer_roofline(r, hbm):
+    return {"bound": "hbm", "bytes_per_step": r["layer_bytes"],
+            "achieved": r["layer_bytes"] / (r["ms"] * 1e-3) / 1e9,
+            "frac": r["layer_bytes"] / (r["ms"] * 1e-3) / 1e9 / hbm,
+            "w13_gemm_ms": r["w13_ms"], "w2_gemm_ms": r["w2_ms"],
+            "w2_gbs": r["w2_bytes"] / (r["w2_ms"] * 1e-3) / 1e9,
+            "w2_frac": r["w2_bytes"] / (r["w2_ms"] * 1e-3) / 1e9 / hbm}
 
 
 def main_ep(args, dev, rank, world, hbm):
     import torch.distributed as dist
-    dec = run_ep(DECODE_M, None, args.steps, args.warmup, dev, rank, world, sample_clocks=(rank == 0),
-                 soak_steps=300)
-    pre = None
+    dec = run_ep(DECODE_M, "bias", args.steps, args.warmup, dev, rank, world, soak_steps=300)
+    pre = {}
     if not args.no_prefill:
-        pre = run_ep(EP_PREFILL_TOKENS // world, 1.1, max(3, args.steps // 20), args.warmup, dev, rank,
-                     world, sample_clocks=False)
+        for kind in ("zipf", "uniform"):
+            pre[kind] = run_ep(EP_PREFILL_TOKENS // world, kind, max(3, args.steps // 20),
+                               args.warmup, dev, rank, world, soak_steps=20)
     if rank == 0:
         total = DECODE_M * world
+        achieved = dec["weight_bytes_touched"] / (dec["ms"] * 1e-3) / 1e9
         line = {
             "metric": "MoE layer tokens/s (decode M=64)",
             "value": total / (dec["ms"] * 1e-3),
@@ -593,26 +755,33 @@ def main_ep(args, dev, rank, world, hbm):
             "config": {"workload": "decode MoE layer, expert parallel: H=7168 I=2048 E=256 top-8, "
                                    f"M=64 tokens per GPU, {E // world} experts per GPU",
                        "parallelism": f"ep{world}", "l2": "not flushed: weights streamed per step",
-                       "collectives": "NCCL all_to_all_single (counts, int8 rows + metadata, "
-                                      "bf16 partials)",
-                       "rank0_dispatch": dec["stats"]},
+                       "collectives": "NCCL all_to_all_single: one packed exchange of int8 rows "
+                                      "+ metadata (fixed capacity, no host sync), one of bf16 "
+                                      "partials",
+                       "rank0_dispatch": dec["stats"], "phases_ms_max_over_ranks": dec["phases_ms"]},
             "roofline": {"bound": "hbm", "kernel": "whole EP layer step (rank 0)",
-                         "achieved": dec["weight_bytes_local"] / (dec["ms"] * 1e-3) / 1e9,
-                         "peak": hbm, "unit": "GB/s",
-                         "frac": dec["weight_bytes_local"] / (dec["ms"] * 1e-3) / 1e9 / hbm,
-                         "traffic": None, "note": "upper bound: all local experts counted"},
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "note": "weight bytes of the experts rank 0 touched "
+                                 f"({dec['touched_rank0']} of {dec['e_loc']})"},
             "e2e": {"value": total / (dec["e2e_ms"] * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"],
                     "ms_per_step": dec["e2e_ms"]},
             "gpu_launches": (LAUNCHES_PER_STEP + 3) * args.steps,
             "clocks": dec["clocks"],
         }
-        if pre is not None:
-            line["prefill"] = {"workload": f"EP prefill: {EP_PREFILL_TOKENS} tokens total, Zipf(1.1)",
-                               "value": EP_PREFILL_TOKENS / (pre["ms"] * 1e-3), "unit": "tokens/s",
-                               "ms_per_step": pre["ms"],
-                               "e2e": {"value": EP_PREFILL_TOKENS / (pre["e2e_ms"] * 1e-3),
-                                       "unit": "tokens/s"}}
+        for kind, r in pre.items():
+            line[f"prefill_{kind}"] = {
+                "workload": f"EP prefill (BASELINE configs[4]): {EP_PREFILL_TOKENS} tokens in "
+                            f"total, {EP_PREFILL_TOKENS // world} per GPU, {kind} routing",
+                "scaling": "strong",
+                "value": EP_PREFILL_TOKENS / (r["ms"] * 1e-3), "unit": "tokens/s",
+                "ms_per_step": r["ms"], "phases_ms_max_over_ranks": r["phases_ms"],
+                "rank0_dispatch": r["stats"],
+                "e2e": {"value": EP_PREFILL_TOKENS / (r["e2e_ms"] * 1e-3), "unit": "tokens/s",
+                        "ms_per_step": r["e2e_ms"], "h2d_bytes_per_step": r["h2d"],
+                        "d2h_bytes_per_step": r["d2h"]},
+                "clocks": r["clocks"]}
         print(json.dumps(line))
     dist.barrier()
     dist.destroy_process_group()

@@ -626,12 +626,14 @@ int dsv4_b200_mxfp4_int8_moe_gemm_swiglu(
 // ---- expert-sorted row pipeline ----
 
 int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, int64_t m_in, int64_t k,
-                            const int32_t* sorted_token_ids, int64_t sorted_capacity,
+                            int64_t lda, int64_t scale_stride, const int32_t* sorted_token_ids, int64_t sorted_capacity,
                             const int32_t* num_tokens_post_padded, int64_t topk,
                             int source_rows_are_slots, int64_t num_valid_tokens, int8_t* out_q,
                             float* out_scale, int32_t* out_rowsum, void* stream) {
   if (int r = ensure_init()) return r;
   DSV4_REQUIRE(m_in >= 0 && k > 0 && k % 128 == 0, "K must be a positive multiple of 128");
+  DSV4_REQUIRE(lda >= k && lda % 16 == 0 && scale_stride >= 1,
+               "lda must be a multiple of 16 and >= K; scale_stride >= 1");
   DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
   DSV4_REQUIRE(num_valid_tokens >= 0 && num_valid_tokens < (1ll << 31), "bad num_valid_tokens");
   if (sorted_capacity == 0 || m_in == 0) return DSV4_OK;
@@ -643,7 +645,8 @@ int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, int64_t m_i
                "a_q and out_q must be 16-byte aligned");
   const int64_t blocks = (sorted_capacity + 7) / 8 < 4096 ? (sorted_capacity + 7) / 8 : 4096;
   sort_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
-      a_q, a_scale, m_in, k, sorted_token_ids, num_tokens_post_padded, sorted_capacity,
+      a_q, a_scale, m_in, k, lda, scale_stride, sorted_token_ids, num_tokens_post_padded,
+      sorted_capacity,
       static_cast<int>(topk), source_rows_are_slots ? 1 : 0, static_cast<int>(num_valid_tokens),
       out_q, out_scale, out_rowsum);
   return check_launch("sort_rows_kernel");
@@ -758,37 +761,41 @@ int dsv4_b200_mxfp4_int8_moe_reduce_masked(const void* routed_out, const float* 
 }
 
 int dsv4_b200_gather_rows(const void* src, int64_t row_bytes, const int64_t* idx, int64_t n_rows,
-                          void* dst, void* stream) {
+                          void* dst, int64_t dst_stride, void* stream) {
   if (int r = ensure_init()) return r;
   DSV4_REQUIRE(row_bytes > 0 && row_bytes % 16 == 0, "row_bytes must be a multiple of 16");
+  DSV4_REQUIRE(dst_stride >= row_bytes && dst_stride % 16 == 0,
+               "dst_stride must be a multiple of 16 and >= row_bytes");
   DSV4_REQUIRE(n_rows >= 0, "bad n_rows");
   if (n_rows == 0) return DSV4_OK;
-  DSV4_REQUIRE(src && idx && dst, "null pointer argument");
+  DSV4_REQUIRE(idx && dst, "null pointer argument");
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0,
                "rows must be 16-byte aligned");
   const int64_t total = n_rows * (row_bytes / 16);
   const int64_t blocks = (total + 255) / 256 < 65535 ? (total + 255) / 256 : 65535;
   gather_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
-      static_cast<const uint8_t*>(src), row_bytes, idx, n_rows, static_cast<uint8_t*>(dst));
+      static_cast<const uint8_t*>(src), row_bytes, idx, n_rows, static_cast<uint8_t*>(dst),
+      dst_stride);
   return check_launch("gather_rows_kernel");
 }
 
 int dsv4_b200_ep_plan_fixed(const int32_t* topk_ids, const float* topk_weights,
                             const float* a_scale, int64_t m, int64_t topk, int64_t num_experts,
                             int64_t world, int64_t capacity, int64_t* send_src,
-                            int32_t* send_meta, int64_t meta_words, int64_t* pos, void* stream) {
+                            int32_t* send_meta, int64_t meta_words, int64_t meta_stride,
+                            int64_t* pos, void* stream) {
   if (int r = ensure_init()) return r;
   DSV4_REQUIRE(world >= 1 && world <= 8 && num_experts % world == 0,
                "world must be in [1, 8] and divide num_experts");
-  DSV4_REQUIRE(m >= 0 && m <= capacity && capacity <= kEpPlanThreads,
-               "need m <= capacity <= %d", kEpPlanThreads);
-  DSV4_REQUIRE(topk >= 1 && topk <= 8 && meta_words >= 1 + 2 * topk, "bad topk / meta width");
-  DSV4_REQUIRE(send_src && send_meta && pos && (m == 0 || (topk_ids && topk_weights && a_scale)),
+  DSV4_REQUIRE(m >= 0 && m <= capacity && capacity < (1ll << 30), "need 0 <= m <= capacity");
+  DSV4_REQUIRE(topk >= 1 && topk <= 8 && meta_words >= 1 + 2 * topk && meta_stride >= meta_words,
+               "bad topk / meta width / meta stride");
+  DSV4_REQUIRE(send_src && send_meta && (m == 0 || (topk_ids && topk_weights && a_scale && pos)),
                "null pointer argument");
   ep_plan_fixed_kernel<<<1, kEpPlanThreads, 0, as_stream(stream)>>>(
       topk_ids, topk_weights, a_scale, static_cast<int>(m), static_cast<int>(topk),
       static_cast<int>(num_experts), static_cast<int>(world), static_cast<int>(capacity),
-      send_src, send_meta, static_cast<int>(meta_words), pos);
+      send_src, send_meta, static_cast<int>(meta_words), meta_stride, pos);
   return check_launch("ep_plan_fixed_kernel");
 }
 

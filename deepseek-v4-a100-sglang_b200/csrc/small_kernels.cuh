@@ -182,10 +182,13 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
 // holding routed slot s (< num_valid) receives row (s / topk, or s when the
 // rows are slots) of a_q and its scale, K-chunk-major [K/128][cap][128].
 // Padding positions are left unwritten (their MMA columns are never stored).
-// One warp per position, 16 B per lane.
+// Source rows are lda bytes apart and their scales scale_stride floats apart
+// (rows received packed with their metadata).  One warp per position, 16 B
+// per lane.
 __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict__ a,
                                                         const float* __restrict__ a_scale,
                                                         int64_t a_rows, int64_t k,
+                                                        int64_t lda, int64_t scale_stride,
                                                         const int32_t* __restrict__ sorted,
                                                         const int32_t* __restrict__ ntpp,
                                                         int64_t cap, int topk, int src_is_slot,
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
     if (slot < 0 || slot >= num_valid) continue;
     const int64_t src = src_is_slot ? slot : slot / topk;
     if (src >= a_rows) continue;
-    const int4* row = reinterpret_cast<const int4*>(a + src * k);
+    const int4* row = reinterpret_cast<const int4*>(a + src * lda);
     int sum = 0;
     for (int c = lane; c < nv; c += 32) {
       const int4 v = __ldg(row + c);
@@ -212,7 +215,7 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (lane == 0) {
-      out_scale[pos] = __ldg(a_scale + src);
+      out_scale[pos] = __ldg(a_scale + src * scale_stride);
       out_rowsum[pos] = sum;
     }
   }
@@ -552,10 +555,11 @@ __global__ void moe_reduce_masked_kernel(const __nv_bfloat16* __restrict__ route
   reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * n)[c] = *reinterpret_cast<uint4*>(o);
 }
 
-// Row gather: dst[i] = src[idx[i]] for rows of row_bytes (multiple of 16).
+// Row gather: dst row i (dst_stride bytes apart) = src[idx[i]] (row_bytes,
+// a multiple of 16), or zeros where idx[i] < 0.
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, int64_t row_bytes,
                                    const int64_t* __restrict__ idx, int64_t n_rows,
-                                   uint8_t* __restrict__ dst) {
+                                   uint8_t* __restrict__ dst, int64_t dst_stride) {
   const int64_t vec = row_bytes / 16;
   const int64_t total = n_rows * vec;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -563,8 +567,9 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, int64_t row_
     const int64_t r = i / vec;
     const int64_t c = i - r * vec;
     const int64_t s = __ldg(idx + r);
-    reinterpret_cast<uint4*>(dst + r * row_bytes)[c] =
-        __ldg(reinterpret_cast<const uint4*>(src + s * row_bytes) + c);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (s >= 0) v = __ldg(reinterpret_cast<const uint4*>(src + s * row_bytes) + c);
+    reinterpret_cast<uint4*>(dst + r * dst_stride)[c] = v;
   }
 }
 
@@ -601,63 +606,79 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* __restrict__ partial,
   reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * n)[c] = *reinterpret_cast<uint4*>(o);
 }
 
-// Expert-parallel plan for the fixed-capacity exchange (one CTA, m <= 1024
-// tokens, world <= 8).  For token t and rank r holding one of its experts,
+// Expert-parallel plan for the fixed-capacity exchange (one CTA, any m <=
+// capacity, world <= 8).  For token t and rank r holding one of its experts,
 // the row goes to slot r*capacity + (number of earlier tokens that also go to
-// r).  Outputs, per slot: the source token (0 for padding), a metadata row
-// {scale, topk local expert ids (-1 = not on r / padding), topk weights};
-// per token: pos[t][r] = slot or -1.
+// r).  Tokens are taken 1024 at a time; per-rank running counts carry over.
+// Outputs, per slot: the source token (-1 for padding) and a metadata row
+// {scale, topk local expert ids (-1 = not on r / padding), topk weights}
+// written at meta + slot * meta_stride (int32 words, so the rows can sit in
+// the tail of the packed send rows); per token: pos[t][r] = slot or -1.
 constexpr int kEpPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kEpPlanThreads, 1)
 ep_plan_fixed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w,
                      const float* __restrict__ a_scale, int m, int topk, int num_experts,
                      int world, int capacity, int64_t* __restrict__ send_src,
-                     int32_t* __restrict__ meta, int meta_words, int64_t* __restrict__ pos) {
+                     int32_t* __restrict__ meta, int meta_words, int64_t meta_stride,
+                     int64_t* __restrict__ pos) {
   __shared__ int warp_cnt[8][32];
-  const int t = threadIdx.x;
-  const int lane = t & 31, wid = t >> 5;
+  __shared__ int run[8];
+  const int t0 = threadIdx.x;
+  const int lane = t0 & 31, wid = t0 >> 5;
   const int e_loc = num_experts / world;
   // padding defaults for every slot
-  for (int sidx = t; sidx < world * capacity; sidx += kEpPlanThreads) {
-    send_src[sidx] = 0;
-    int32_t* row = meta + static_cast<int64_t>(sidx) * meta_words;
+  for (int sidx = t0; sidx < world * capacity; sidx += kEpPlanThreads) {
+    send_src[sidx] = -1;
+    int32_t* row = meta + static_cast<int64_t>(sidx) * meta_stride;
     for (int c = 0; c < meta_words; ++c) row[c] = (c >= 1 && c <= topk) ? -1 : 0;
   }
-  uint32_t has = 0;
-  if (t < m) {
-    for (int k = 0; k < topk; ++k) {
-      const int e = ids[t * topk + k];
-      if (e >= 0 && e < num_experts) has |= 1u << (e / e_loc);
-    }
-  }
-  int rank_in[8];
-  for (int r = 0; r < world; ++r) {
-    const unsigned b = __ballot_sync(0xffffffffu, (has >> r) & 1u);
-    rank_in[r] = __popc(b & ((1u << lane) - 1u));
-    if (lane == 0) warp_cnt[r][wid] = __popc(b);
-  }
+  if (t0 < 8) run[t0] = 0;
   __syncthreads();
-  if (t < m) {
-    for (int r = 0; r < world; ++r) {
-      int64_t slot = -1;
-      if ((has >> r) & 1u) {
-        int before = 0;
-        for (int q = 0; q < wid; ++q) before += warp_cnt[r][q];
-        const int j = before + rank_in[r];
-        slot = static_cast<int64_t>(r) * capacity + j;
-        send_src[slot] = t;
-        int32_t* row = meta + slot * meta_words;
-        row[0] = __float_as_int(a_scale[t]);
-        for (int k = 0; k < topk; ++k) {
-          const int e = ids[t * topk + k];
-          const bool mine = e >= 0 && e < num_experts && e / e_loc == r;
-          row[1 + k] = mine ? e - r * e_loc : -1;
-          row[1 + topk + k] = __float_as_int(mine ? w[t * topk + k] : 0.f);
-        }
+  for (int base = 0; base < m; base += kEpPlanThreads) {
+    const int t = base + t0;
+    uint32_t has = 0;
+    if (t < m) {
+      for (int k = 0; k < topk; ++k) {
+        const int e = ids[static_cast<int64_t>(t) * topk + k];
+        if (e >= 0 && e < num_experts) has |= 1u << (e / e_loc);
       }
-      pos[static_cast<int64_t>(t) * world + r] = slot;
     }
+    int rank_in[8];
+    for (int r = 0; r < world; ++r) {
+      const unsigned b = __ballot_sync(0xffffffffu, (has >> r) & 1u);
+      rank_in[r] = __popc(b & ((1u << lane) - 1u));
+      if (lane == 0) warp_cnt[r][wid] = __popc(b);
+    }
+    __syncthreads();
+    if (t < m) {
+      for (int r = 0; r < world; ++r) {
+        int64_t slot = -1;
+        if ((has >> r) & 1u) {
+          int before = run[r];
+          for (int q = 0; q < wid; ++q) before += warp_cnt[r][q];
+          const int j = before + rank_in[r];
+          slot = static_cast<int64_t>(r) * capacity + j;
+          send_src[slot] = t;
+          int32_t* row = meta + slot * meta_stride;
+          row[0] = __float_as_int(a_scale[t]);
+          for (int k = 0; k < topk; ++k) {
+            const int e = ids[static_cast<int64_t>(t) * topk + k];
+            const bool mine = e >= 0 && e < num_experts && e / e_loc == r;
+            row[1 + k] = mine ? e - r * e_loc : -1;
+            row[1 + topk + k] = __float_as_int(mine ? w[static_cast<int64_t>(t) * topk + k] : 0.f);
+          }
+        }
+        pos[static_cast<int64_t>(t) * world + r] = slot;
+      }
+    }
+    __syncthreads();
+    if (t0 < world) {
+      int tot = 0;
+      for (int q = 0; q < 32; ++q) tot += warp_cnt[t0][q];
+      run[t0] += tot;
+    }
+    __syncthreads();
   }
 }
 

@@ -40,7 +40,7 @@ SIGNATURES: dict[str, list] = {
                                              _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I,
                                              _F, _P],
     "dsv4_b200_router_topk": [_P, _I, _I64, _I64, _P, _I64, _I, _F, _P, _P, _P],
-    "dsv4_b200_moe_sort_rows": [_P, _P, _I64, _I64, _P, _I64, _P, _I64, _I, _I64, _P, _P, _P,
+    "dsv4_b200_moe_sort_rows": [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I, _I64, _P, _P, _P,
                                 _P],
     "dsv4_b200_quantize_sorted_int8": [_P, _I, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P],
     "dsv4_b200_mxfp4_int8_moe_gemm_sorted": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
@@ -50,8 +50,9 @@ SIGNATURES: dict[str, list] = {
                                                     _I64, _I64, _I, _F, _P],
     "dsv4_b200_mxfp4_int8_moe_reduce": [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P],
     "dsv4_b200_mxfp4_int8_moe_reduce_masked": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P],
-    "dsv4_b200_gather_rows": [_P, _I64, _P, _I64, _P, _P],
-    "dsv4_b200_ep_plan_fixed": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P],
+    "dsv4_b200_gather_rows": [_P, _I64, _P, _I64, _P, _I64, _P],
+    "dsv4_b200_ep_plan_fixed": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _P,
+                                _P],
     "dsv4_b200_ep_combine": [_P, _P, _I64, _P, _I64, _I64, _I, _F, _P],
     "dsv4_b200_mxfp4_int8_dense_gemm": [_P, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _P,
                                         _I64, _I64, _P],

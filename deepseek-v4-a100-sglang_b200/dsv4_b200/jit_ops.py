@@ -171,19 +171,24 @@ def moe_sort_rows(a_q, a_scale, sorted_token_ids, num_tokens_post_padded, *, top
     ``[K/128][sorted_capacity][128]`` (flat), ``scale`` fp32 and ``rowsum``
     int32 (sum of the row's int8 values) ``[sorted_capacity]``; position p
     holds row ``sorted_token_ids[p] // topk`` (or the slot itself).  Padding
-    positions are left unwritten."""
-    _check_tensor(a_q, "a_q", torch.int8, device=a_q.device)
-    _check_tensor(a_scale, "a_scale", torch.float32, (a_q.shape[0],), a_q.device)
-    k = a_q.shape[1]
+    positions are left unwritten.  ``a_q`` may be a row-strided view (rows
+    16-byte aligned) and ``a_scale`` a strided 1-D view, as when the rows
+    arrive packed with their metadata."""
+    _check(a_q.is_cuda and a_q.dtype == torch.int8 and a_q.dim() == 2 and a_q.stride(1) == 1,
+           "a_q must be a CUDA int8 [M, K] tensor with unit column stride")
+    _check(a_scale.is_cuda and a_scale.dtype == torch.float32 and a_scale.dim() == 1
+           and a_scale.shape[0] == a_q.shape[0], "a_scale must be a CUDA fp32 [M] tensor")
+    m_in, k = a_q.shape
+    lda = a_q.stride(0) if m_in > 1 else k
     cap = sorted_token_ids.numel()
     q = torch.empty(cap * k, device=a_q.device, dtype=torch.int8)
     sc = torch.empty(cap, device=a_q.device, dtype=torch.float32)
     rs = torch.empty(cap, device=a_q.device, dtype=torch.int32)
     _init_device(a_q.device)
-    N.call("dsv4_b200_moe_sort_rows", a_q.data_ptr(), a_scale.data_ptr(), a_q.shape[0], k,
-           sorted_token_ids.data_ptr(), cap, num_tokens_post_padded.data_ptr(), topk,
-           1 if source_rows_are_slots else 0, num_valid_tokens, q.data_ptr(), sc.data_ptr(),
-           rs.data_ptr(), N.stream_of(a_q))
+    N.call("dsv4_b200_moe_sort_rows", a_q.data_ptr(), a_scale.data_ptr(), m_in, k, lda,
+           max(a_scale.stride(0), 1), sorted_token_ids.data_ptr(), cap,
+           num_tokens_post_padded.data_ptr(), topk, 1 if source_rows_are_slots else 0,
+           num_valid_tokens, q.data_ptr(), sc.data_ptr(), rs.data_ptr(), N.stream_of(a_q))
     return q, sc, rs
 
 

@@ -356,11 +356,15 @@ def mxfp4_int8_moe_forward_quantized(a_q: torch.Tensor, a_scale: torch.Tensor,
                                      topk_weights: torch.Tensor, *, hidden_size: int,
                                      intermediate_size: int,
                                      routed_scaling_factor: float | None = None,
-                                     clamp_limit: float | None = None) -> torch.Tensor:
+                                     clamp_limit: float | None = None,
+                                     expected_routes: int | None = None) -> torch.Tensor:
     """MoE layer on rows that are already INT8-quantised (``a_q``, ``a_scale``),
     as they arrive from the expert-parallel dispatch.  ``topk_ids`` index the
     local experts of ``weights``; negative ids (experts held by other ranks)
-    contribute nothing.  Same arithmetic as mxfp4_int8_moe_forward."""
+    contribute nothing.  Same arithmetic as mxfp4_int8_moe_forward.
+    ``expected_routes``: the number of valid (id >= 0) routes the caller
+    expects, for the token-tile choice when many rows are padding (the exact
+    count would need a host synchronisation); default: every route."""
     _require_cuda(a_q, "a_q")
     ids = topk_ids.to(torch.int32).contiguous()
     w = topk_weights.to(torch.float32).contiguous()
@@ -368,10 +372,11 @@ def mxfp4_int8_moe_forward_quantized(a_q: torch.Tensor, a_scale: torch.Tensor,
     experts = weights.w13_mxfp4.shape[0]
     if m == 0:
         return torch.empty((0, hidden_size), device=a_q.device, dtype=torch.bfloat16)
-    _, block_n = _select_moe_tile_shape(m, topk, experts)
-    block_m = select_sorted_block_m(m, topk, experts)
+    m_sel = m if expected_routes is None else max(1, -(-int(expected_routes) // topk))
+    _, block_n = _select_moe_tile_shape(m_sel, topk, experts)
+    block_m = select_sorted_block_m(m_sel, topk, experts)
     sorted_ids, expert_ids, ntpp = moe_align_block_size(ids, block_m, experts)
-    return _moe_core(a_q.contiguous(), a_scale.contiguous(), weights, ids, w, sorted_ids,
+    return _moe_core(a_q, a_scale, weights, ids, w, sorted_ids,
                      expert_ids, ntpp, block_m=block_m, block_n=block_n, hidden_size=hidden_size,
                      intermediate_size=intermediate_size,
                      routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,

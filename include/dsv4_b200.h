@@ -153,9 +153,13 @@ DSV4_API int dsv4_b200_mxfp4_int8_moe_gemm_swiglu(
  * dsv4_b200_moe_sort_rows: out_q[pos] = a_q[src(slot)], out_scale[pos] =
  *   a_scale[src(slot)], out_rowsum[pos] = sum_k a_q[src][k], src = slot /
  *   topk (or slot when source_rows_are_slots).  The per-token INT8 rows of
- *   PYMOE:904-909 in the order of the aligned permutation (PYMOE:842-869). */
+ *   PYMOE:904-909 in the order of the aligned permutation (PYMOE:842-869).
+ *   Source rows are lda bytes apart (>= k, multiple of 16) and their scales
+ *   scale_stride floats apart (k and 1 for plain [m_in, k] / [m_in] tensors;
+ *   larger for rows received packed with their metadata). */
 DSV4_API int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, int64_t m_in,
-                                     int64_t k, const int32_t* sorted_token_ids,
+                                     int64_t k, int64_t lda, int64_t scale_stride,
+                                     const int32_t* sorted_token_ids,
                                      int64_t sorted_capacity,
                                      const int32_t* num_tokens_post_padded, int64_t topk,
                                      int source_rows_are_slots, int64_t num_valid_tokens,
@@ -216,25 +220,27 @@ DSV4_API int dsv4_b200_mxfp4_int8_moe_reduce_masked(const void* routed_out,
                                                     int64_t num_valid_tokens, int apply_scaling,
                                                     float routed_scaling_factor, void* stream);
 
-/* Expert-parallel dispatch packing: dst[i] = src[idx[i]] for rows of
- * row_bytes (multiple of 16, 16-byte aligned rows).  New component: the
- * reference has no expert parallelism. */
+/* Expert-parallel dispatch packing: row i of dst (dst_stride bytes apart)
+ * = src[idx[i]] (rows of row_bytes, a multiple of 16, 16-byte aligned), or
+ * zeros where idx[i] < 0 (padding; src may then be null when every index is
+ * negative).  New component: the reference has no expert parallelism. */
 DSV4_API int dsv4_b200_gather_rows(const void* src, int64_t row_bytes, const int64_t* idx,
-                                   int64_t n_rows, void* dst, void* stream);
+                                   int64_t n_rows, void* dst, int64_t dst_stride, void* stream);
 
 /* Expert-parallel plan for the fixed-capacity exchange (new component: the
- * reference has no expert parallelism).  For each token t (m <= capacity <=
- * 1024) and each rank r (world <= 8, experts split contiguously) that holds
- * one of its top-k experts: slot r*capacity + (earlier tokens bound for r).
- * Writes send_src [world*capacity] (token per slot, 0 for padding),
- * send_meta int32 [world*capacity][meta_words] = {scale bits, topk local
- * expert ids (-1 = elsewhere / padding), topk weight bits}, and
- * pos int64 [m][world] (slot or -1). */
+ * reference has no expert parallelism).  For each token t (m <= capacity)
+ * and each rank r (world <= 8, experts split contiguously) that holds one of
+ * its top-k experts: slot r*capacity + (earlier tokens bound for r).  Writes
+ * send_src [world*capacity] (token per slot, -1 for padding), the metadata
+ * row of each slot at send_meta + slot * meta_stride int32 words = {scale
+ * bits, topk local expert ids (-1 = elsewhere / padding), topk weight bits}
+ * (meta_words words; meta_stride >= meta_words lets the rows sit in the
+ * tail of packed send rows), and pos int64 [m][world] (slot or -1). */
 DSV4_API int dsv4_b200_ep_plan_fixed(const int32_t* topk_ids, const float* topk_weights,
                                      const float* a_scale, int64_t m, int64_t topk,
                                      int64_t num_experts, int64_t world, int64_t capacity,
                                      int64_t* send_src, int32_t* send_meta, int64_t meta_words,
-                                     int64_t* pos, void* stream);
+                                     int64_t meta_stride, int64_t* pos, void* stream);
 
 /* Expert-parallel combine: out[t] = bf16(sum over r = 0..world-1, in rank
  * order, of f32(partial[pos[t][r]])) for pos >= 0, then optional routed

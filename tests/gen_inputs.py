@@ -45,17 +45,24 @@ def routing_softmax_topk(tokens, experts, topk, seed):
     return ids.to(torch.int32), w.to(torch.float32)
 
 
-def routing_sigmoid_bias_topk(tokens, experts, topk, seed, *, zipf_s=None):
+def routing_sigmoid_bias_topk(tokens, experts, topk, seed, *, zipf_s=None, model_seed=None):
     """DeepSeek-style routing: sigmoid scores, per-expert bias N(0, 0.1) used
     for selection only, weights = chosen sigmoid scores renormalised to sum 1.
     With ``zipf_s`` the logits get ``log p_e`` added, ``p_e ~ rank^-s`` over a
-    seeded expert permutation (skewed expert popularity)."""
+    seeded expert permutation (skewed expert popularity).  With
+    ``model_seed`` the bias and the popularity permutation (properties of the
+    model, shared by every rank) come from that seed and only the logits from
+    ``seed``."""
     gen = torch.Generator()
     gen.manual_seed(seed)
     logits = torch.randn(tokens, experts, generator=gen)
-    bias = torch.randn(experts, generator=gen) * 0.1
+    mgen = gen
+    if model_seed is not None:
+        mgen = torch.Generator()
+        mgen.manual_seed(model_seed)
+    bias = torch.randn(experts, generator=mgen) * 0.1
     if zipf_s is not None:
-        perm = torch.randperm(experts, generator=gen)
+        perm = torch.randperm(experts, generator=mgen)
         ranks = torch.empty(experts)
         ranks[perm] = torch.arange(1, experts + 1, dtype=torch.float32)
         p = ranks.pow(-zipf_s)
@@ -66,6 +73,17 @@ def routing_sigmoid_bias_topk(tokens, experts, topk, seed, *, zipf_s=None):
     w = torch.gather(scores, 1, ids)
     w = w / w.sum(dim=-1, keepdim=True)
     return ids.to(torch.int32), w.to(torch.float32)
+
+
+def routing_uniform_topk(tokens, experts, topk, seed):
+    """Uniform routing: top-k of sigmoid(N(0,1)) logits with no bias or skew
+    (every expert equally likely), weights renormalised to sum 1."""
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+    scores = torch.sigmoid(torch.randn(tokens, experts, generator=gen))
+    _, ids = torch.topk(scores, topk, dim=-1)
+    w = torch.gather(scores, 1, ids)
+    return ids.to(torch.int32), (w / w.sum(dim=-1, keepdim=True)).to(torch.float32)
 
 
 def round_robin_routing(tokens, experts, topk):

@@ -51,7 +51,7 @@ class CpuOracleOps:
     def gather_rows(self, rows, idx):
         return rows.index_select(0, idx).contiguous()
 
-    def local_moe(self, a_q, a_scale, lids, w):
+    def local_moe(self, a_q, a_scale, lids, w, expected_routes=None):
         m, topk = lids.shape
         if m == 0:
             return torch.empty((0, H), dtype=torch.bfloat16)
@@ -79,7 +79,7 @@ class CpuOracleOps:
         return torch.from_numpy(O.f32_to_bf16_bits(acc).view(np.int16)).view(torch.bfloat16)
 
 
-def _worker(rank, world, port, q, capacity=None):
+def _worker(rank, world, port, q, mode="fixed", zero_rank=-1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -89,8 +89,11 @@ def _worker(rank, world, port, q, capacity=None):
         e_loc = E // world
         local = {k: v[rank * e_loc:(rank + 1) * e_loc] for k, v in full.items()}
         ep = ExpertParallelMoE(CpuOracleOps(local), num_experts=E, hidden_size=H,
-                               capacity_tokens=capacity)
+                               capacity_tokens=M if mode == "fixed" else None,
+                               exact_sizes=(mode == "exact"))
         x, ids, w = _inputs(rank)
+        if rank == zero_rank:  # this rank has no tokens this step
+            x, ids, w = x[:0], ids[:0], w[:0]
         out = ep.forward(x, ids, w)
         q.put((rank, out.view(torch.int16).numpy().copy(), ep.last_stats))
     finally:
@@ -126,13 +129,17 @@ def test_plan_bookkeeping_exact():
     assert (plan.send_rank.diff() >= 0).all()
 
 
-@pytest.mark.parametrize("capacity", [None, M])
-def test_ep_world2_matches_single_process_oracle(capacity):
+@pytest.mark.parametrize("mode,zero_rank", [("exact", -1), ("fixed", -1), ("implicit", -1),
+                                            ("exact", 1), ("fixed", 1), ("fixed", 0)])
+def test_ep_world2_matches_single_process_oracle(mode, zero_rank):
+    """Packed single-exchange dispatch in every size mode; a rank with zero
+    tokens still takes part in every collective (ranks that get no rows)."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, capacity)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode, zero_rank))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -144,9 +151,11 @@ def test_ep_world2_matches_single_process_oracle(capacity):
         assert p.exitcode == 0
     full = _weights()
     for rank in range(world):
+        if rank == zero_rank:
+            assert res[rank][0].shape == (0, H)
+            continue
         x, ids, w = _inputs(rank)
         ref = O.moe_forward(x.view(torch.int16).numpy().view(np.uint16), full, ids.numpy(), w.numpy(),
                             block_m=16)
         got = O.bf16_bits_to_f32(res[rank][0].view(np.uint16))
         assert O.relative_l2(got, O.bf16_bits_to_f32(ref)) < 1e-2
-        assert res[rank][1]["recv_rows"] > 0

@@ -25,7 +25,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, capacity):
+def _worker(rank, world, port, q, mode, zero_rank):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "deepseek-v4-a100-sglang_b200"), os.path.join(root, "tests")]
@@ -47,8 +47,17 @@ def _worker(rank, world, port, q, capacity):
         x = G.randn_bf16((M, H), 500 + rank).to(dev)
         ids, tw = G.routing_sigmoid_bias_topk(M, E, TOPK, 600 + rank)
         ep = ExpertParallelMoE(GpuOps(lw, H, I), num_experts=E, hidden_size=H, routed_scaling_factor=2.0,
-                               capacity_tokens=capacity)
+                               capacity_tokens=M if mode == "fixed" else None,
+                               exact_sizes=(mode == "exact"), timing=True)
+        if rank == zero_rank:  # no tokens on this rank this step
+            x, ids, tw = x[:0], ids[:0], tw[:0]
         out = ep.forward(x, ids.to(dev), tw.to(dev))
+        phases = ep.phase_ms()
+        assert set(phases) == set(ep.PHASES)
+        D.check_device_status()
+        if rank == zero_rank:
+            q.put((rank, 0.0 if out.shape == (0, H) else 1.0))
+            return
         ref = D.mxfp4_int8_moe_forward(x, fw, ids.to(dev), tw.to(dev), hidden_size=H,
                                        intermediate_size=I, routed_scaling_factor=2.0)
         rel = float((out.float() - ref.float()).norm() / ref.float().norm())
@@ -58,13 +67,15 @@ def _worker(rank, world, port, q, capacity):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("capacity", [None, M])
-def test_ep_nccl_matches_single_gpu(capacity):
+@pytest.mark.parametrize("mode,zero_rank", [("exact", -1), ("fixed", -1), ("implicit", -1),
+                                            ("fixed", 1), ("exact", 0)])
+def test_ep_nccl_matches_single_gpu(mode, zero_rank):
     world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, capacity)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode, zero_rank))
+             for r in range(world)]
     for p in procs:
         p.start()
     rels = [q.get(timeout=300) for _ in range(world)]

@@ -64,13 +64,7 @@ def weights():
 
 def _routing(m, seed, kind):
     if kind == "uniform":
-        gen = torch.Generator()
-        gen.manual_seed(seed)
-        logits = torch.randn(m, E, generator=gen)
-        scores = torch.sigmoid(logits)
-        _, ids = torch.topk(scores, TOPK, dim=-1)
-        w = torch.gather(scores, 1, ids)
-        return ids.to(torch.int32), (w / w.sum(-1, keepdim=True)).float()
+        return G.routing_uniform_topk(m, E, TOPK, seed)
     return G.routing_sigmoid_bias_topk(m, E, TOPK, seed, zipf_s=1.1 if kind == "zipf" else None)
 
 

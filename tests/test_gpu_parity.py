@@ -375,23 +375,35 @@ def test_device_status_clean_after_suite():
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("m", [1, 37, 64, 256])
-def test_ep_plan_fixed_matches_torch_plan(world, m):
-    """The one-kernel fixed-capacity EP plan equals the torch plan + padding."""
+@pytest.mark.parametrize("m", [0, 1, 37, 64, 256, 3000])
+def test_ep_dispatch_pack_matches_torch_plan(world, m):
+    """The two-kernel fixed-capacity EP plan + packing equals the torch plan
+    + padding: positions, packed int8 rows, metadata words, zero padding rows
+    (ids -1).  m = 3000 crosses the kernel's 1024-token chunks; m = 0 is a
+    rank with no tokens."""
     from dsv4_b200.ep import GpuOps, plan_dispatch, pad_plan, pack_meta, _meta_width
-    e, topk, cap = 64, 8, 256
-    ids, tw = G.routing_sigmoid_bias_topk(m, e, topk, 900 + m)
-    ids[0, 0] = -1
+    from dsv4_b200.ep import packed_row_bytes
+    e, topk, h = 64, 8, 256
+    cap = max(m, 1)
+    ids, tw = G.routing_sigmoid_bias_topk(max(m, 1), e, topk, 900 + m)
+    ids, tw = ids[:m], tw[:m]
+    if m:
+        ids[0, 0] = -1
     a_scale = torch.rand(m) + 0.1
-    ops = GpuOps(None, 128, 128)
-    src, meta, pos = ops.plan_fixed(ids.cuda(), tw.cuda(), a_scale.cuda(), e, world, cap)
+    a_q = torch.randint(-127, 128, (m, h), dtype=torch.int8)
+    ops = GpuOps(None, h, 128)
+    buf, pos = ops.dispatch_pack(a_q.cuda(), a_scale.cuda(), ids.cuda(), tw.cuda(), e, world, cap)
     plan = plan_dispatch(ids, tw, e, world)
     padded = pad_plan(plan, world, cap)
-    ref_meta = torch.zeros((world * cap, _meta_width(topk)), dtype=torch.int32)
+    w = _meta_width(topk)
+    rb = packed_row_bytes(h, topk)
+    ref = torch.zeros((world * cap, rb), dtype=torch.uint8)
+    ref_meta = torch.zeros((world * cap, w), dtype=torch.int32)
     ref_meta[:, 1:1 + topk] = -1
-    ref_meta[padded] = pack_meta(a_scale[plan.send_token], plan.send_lids, plan.send_w)
-    ref_src = torch.zeros(world * cap, dtype=torch.int64)
-    ref_src[padded] = plan.send_token
+    if m:
+        ref_meta[padded] = pack_meta(a_scale[plan.send_token], plan.send_lids, plan.send_w)
+        ref[padded, :h] = a_q[plan.send_token].view(torch.uint8)
+    ref[:, h:h + 4 * w] = ref_meta.view(torch.uint8)
+    got = buf.cpu()
     np.testing.assert_array_equal(pos.cpu().numpy(), plan.pos.numpy())
-    np.testing.assert_array_equal(src.cpu().numpy(), ref_src.numpy())
-    np.testing.assert_array_equal(meta.cpu().numpy(), ref_meta.numpy())
+    np.testing.assert_array_equal(got[:, :h + 4 * w].numpy(), ref[:, :h + 4 * w].numpy())
