@@ -510,6 +510,23 @@ def run_dense(dev, steps, warmup, hbm, tops_i8):
                 evs.append((a, b))
             torch.cuda.synchronize()
             ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+            alt_ms = None
+            if m > 128:
+                # the 128-token row-major tile, for comparison with the chosen
+                # 256-token K-chunk-major tile (2 launches: re-layout + GEMM)
+                os.environ["DSV4_B200_DENSE_CM_MIN_M"] = str(1 << 30)
+                gemm()
+                evs2 = []
+                for _ in range(steps):
+                    flush()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    gemm()
+                    b.record()
+                    evs2.append((a, b))
+                torch.cuda.synchronize()
+                os.environ.pop("DSV4_B200_DENSE_CM_MIN_M")
+                alt_ms = statistics.mean(a.elapsed_time(b) for a, b in evs2)
             # end to end through the public op: pinned host x in, host out back
             hx = x.pin_memory()
             hout = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
@@ -535,7 +552,10 @@ def run_dense(dev, steps, warmup, hbm, tops_i8):
                 "kernel_ms": ms, "tokens_per_s": m / (ms * 1e-3),
                 "algorithmic_bytes": alg, "gbs": gbs, "hbm_frac": gbs / hbm,
                 "tops": tops, "int8_frac": tops / tops_i8, "bound": bound,
-                "launches": 2 if m <= 128 else 1,
+                "launches": 2,
+                "path": "128-token-max tile, split-K + reduce" if m <= 128 else
+                        "256-token K-chunk-major tile (re-layout + GEMM)",
+                "tile128_kernel_ms": alt_ms,
                 "e2e": {"ms": e2e_ms, "tokens_per_s": m / (e2e_ms * 1e-3),
                         "h2d_bytes": m * k * 2, "d2h_bytes": m * n * 2}}
     return {"workload": "dense MXFP4/INT8 GEMM (BASELINE configs[1]): bf16 A [M, 7168] "

@@ -68,6 +68,8 @@ cudaError_t set_attrs_epi() {
 constexpr int kAlignMaxExperts = 1024;
 int align_smem_bytes(int experts) { return (32 * experts + experts + 1 + 32) * 4; }
 
+cudaError_t set_router_align_attrs();
+
 int ensure_init() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -86,6 +88,7 @@ int ensure_init() {
   if (e == cudaSuccess) e = set_attrs_epi<kEpiSwiglu>();
   if (e == cudaSuccess) e = set_attrs_epi<kEpiBf16 | kEpiBiased>();
   if (e == cudaSuccess) e = set_attrs_epi<kEpiSwiglu | kEpiBiased>();
+  if (e == cudaSuccess) e = set_router_align_attrs();
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(reinterpret_cast<void*>(&moe_align_kernel),
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -348,7 +351,11 @@ int dense_tile(int64_t m) {
 int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
                  const uint8_t* b_mxfp4, const uint8_t* b_shift2, int64_t shift_stride,
                  const float* cs, int64_t n, void* out, int32_t* out_i32, int64_t splits,
-                 int64_t ld, int64_t split_stride, int epi, void* stream) {
+                 int64_t ld, int64_t split_stride, int epi, void* stream,
+                 const int32_t* a_rowsum = nullptr) {
+  // a_rowsum set: activations are K-chunk-major [K/128][m][128] with int8 row
+  // sums, 256-token tiles, biased-unsigned decode (the expert-sorted path's
+  // tile, with one "expert")
   if (int r = check_weights(1, n, k, shift_stride)) return r;
   DSV4_REQUIRE(cs == nullptr || (reinterpret_cast<uintptr_t>(cs) & 15) == 0,
                "weight_channel_scale must be 16-byte aligned");
@@ -360,6 +367,7 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   p.dec_one = 1u;
   p.a = a_q;
   p.a_scale = a_scale;
+  p.a_rowsum = a_rowsum;
   p.lda = k;
   p.a_rows = m;
   p.cs = cs;
@@ -373,16 +381,57 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   p.out_i32 = out_i32;
   p.ldo = ld;
   p.split_stride = split_stride;
-  const int tn = dense_tile(m);
+  const bool cm = a_rowsum != nullptr;
+  const int tn = cm ? 256 : dense_tile(m);
   if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, 1, k / 32, shift_stride, n / 8, false, 0,
                                  shift_chunk_rows(p.stages_per_split, tn)))
     return r;
-  if (int r = encode_act_map(p, a_q, m, k, 1, tn)) return r;
+  if (int r = encode_act_map(p, a_q, m, k, cm ? 2 : 1, tn)) return r;
   p.m_tiles = static_cast<int>((m + tn - 1) / tn);
   p.row_tiles = static_cast<int>(n / 128);
   const int64_t max_items = static_cast<int64_t>(p.m_tiles) * p.row_tiles * p.splits;
+  if (cm) return launch_gemm<kEpiBf16 | kEpiBiased>(tn, max_items, p, as_stream(stream));
   if (epi == kEpiI32) return launch_gemm<kEpiI32>(tn, max_items, p, as_stream(stream));
   return launch_gemm<kEpiBf16>(tn, max_items, p, as_stream(stream));
+}
+
+// ---- fused router + align (cooperative launch) ----
+template <typename T>
+const void* router_align_fn_t(int epl) {
+  if (epl <= 1) return reinterpret_cast<const void*>(&router_align_kernel<T, 1>);
+  if (epl <= 2) return reinterpret_cast<const void*>(&router_align_kernel<T, 2>);
+  if (epl <= 4) return reinterpret_cast<const void*>(&router_align_kernel<T, 4>);
+  if (epl <= 8) return reinterpret_cast<const void*>(&router_align_kernel<T, 8>);
+  if (epl <= 16) return reinterpret_cast<const void*>(&router_align_kernel<T, 16>);
+  return reinterpret_cast<const void*>(&router_align_kernel<T, 32>);
+}
+
+const void* router_align_fn(int dtype, int epl) {
+  switch (dtype) {
+    case DSV4_F32: return router_align_fn_t<float>(epl);
+    case DSV4_F16: return router_align_fn_t<__half>(epl);
+    case DSV4_BF16: return router_align_fn_t<__nv_bfloat16>(epl);
+    default: return nullptr;
+  }
+}
+
+cudaError_t set_router_align_attrs() {
+  cudaError_t e = cudaSuccess;
+  for (int dt : {DSV4_F32, DSV4_F16, DSV4_BF16})
+    for (int epl : {1, 2, 4, 8, 16, 32})
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(router_align_fn(dt, epl),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 route_align_smem_bytes(kAlignMaxExperts));
+  return e;
+}
+
+// CTAs of the fused router + align: one per 64 tokens, at most one per SM
+// (co-resident, as the grid-wide barrier needs).
+int64_t router_align_grid(int64_t m) {
+  int64_t g = (m + 63) / 64;
+  if (g < 1) g = 1;
+  return g < sm_count() ? g : sm_count();
 }
 
 // Fixed split-K workspace of dsv4_b200_mxfp4_int8_dense_gemm_noalloc:
@@ -560,6 +609,57 @@ int dsv4_b200_router_topk(const void* logits, int dtype, int64_t m, int64_t num_
 #undef DSV4_RT_E
 #undef DSV4_RT
   return check_launch("router_topk_kernel");
+}
+
+int dsv4_b200_router_align_workspace_words(int64_t m, int64_t num_experts, int64_t* words) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(words != nullptr && m >= 0 && num_experts >= 1, "bad arguments");
+  *words = router_align_grid(m) * num_experts;
+  return DSV4_OK;
+}
+
+int dsv4_b200_router_align(const void* logits, int dtype, int64_t m, int64_t num_experts,
+                           const float* bias, int64_t topk, int renormalize, float scale,
+                           int64_t block_size, int32_t* topk_ids, float* topk_weights,
+                           int32_t* sorted_token_ids, int64_t sorted_capacity,
+                           int32_t* expert_ids, int64_t expert_ids_capacity,
+                           int32_t* num_tokens_post_pad, int32_t* workspace,
+                           int64_t workspace_words, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0 && m < (1ll << 27), "bad m %lld", (long long)m);
+  DSV4_REQUIRE(num_experts >= 1 && num_experts <= kAlignMaxExperts,
+               "num_experts must be in [1, %d]", kAlignMaxExperts);
+  DSV4_REQUIRE(topk >= 1 && topk <= 32 && topk <= num_experts, "topk must be in [1, min(32, E)]");
+  DSV4_REQUIRE(block_size >= 1 && block_size <= 1024, "bad block_size %lld", (long long)block_size);
+  DSV4_REQUIRE(num_tokens_post_pad && (m == 0 || (logits && topk_ids && topk_weights)) &&
+                   (sorted_token_ids || sorted_capacity == 0) &&
+                   (expert_ids || expert_ids_capacity == 0),
+               "null pointer argument");
+  const int64_t numel = m * topk;
+  const int64_t need = align_capacity(numel, num_experts, block_size);
+  DSV4_REQUIRE(sorted_capacity >= need, "sorted_token_ids capacity %lld < %lld",
+               (long long)sorted_capacity, (long long)need);
+  DSV4_REQUIRE(expert_ids_capacity * block_size >= need, "expert_ids capacity too small");
+  const int64_t grid = router_align_grid(m);
+  DSV4_REQUIRE(workspace != nullptr && workspace_words >= grid * num_experts,
+               "workspace needs %lld int32 words", (long long)(grid * num_experts));
+  const int epl = static_cast<int>((num_experts + 31) / 32);
+  int m_i = static_cast<int>(m), e_i = static_cast<int>(num_experts), k_i = static_cast<int>(topk);
+  int bm_i = static_cast<int>(block_size);
+  int tpc = static_cast<int>((m + grid - 1) / grid);
+  int cap_i = static_cast<int>(sorted_capacity), ecap_i = static_cast<int>(expert_ids_capacity);
+  void* args[] = {&logits, &m_i, &e_i, &bias, &k_i, &renormalize, &scale, &bm_i, &tpc,
+                  &topk_ids, &topk_weights, &sorted_token_ids, &cap_i, &expert_ids, &ecap_i,
+                  &num_tokens_post_pad, &workspace};
+  const void* fn = router_align_fn(dtype, epl);
+  if (fn == nullptr)
+    return fail(DSV4_ERR_INVALID_ARGUMENT, "logits must be fp32, fp16, or bf16 (dtype %d)", dtype);
+  cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(static_cast<unsigned>(grid)),
+                                              dim3(kRouteAlignThreads), args,
+                                              route_align_smem_bytes(e_i), as_stream(stream));
+  if (e != cudaSuccess)
+    return fail(DSV4_ERR_CUDA, "router_align_kernel: %s", cudaGetErrorString(e));
+  return DSV4_OK;
 }
 
 int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int64_t num_experts,
@@ -867,6 +967,66 @@ int dsv4_b200_mxfp4_int8_dense_gemm_i32(const int8_t* a_q, int64_t m, int64_t k,
   DSV4_REQUIRE(a_q && b_mxfp4 && b_shift2 && acc, "null pointer argument");
   return dense_common(a_q, nullptr, m, k, b_mxfp4, b_shift2, shift_stride, nullptr, n, nullptr,
                       acc, 1, n, 0, kEpiI32, stream);
+}
+
+int dsv4_b200_quantize_per_token_int8_cm(const void* a, int dtype, int64_t m, int64_t k,
+                                         int8_t* a_cm, float* a_scale, int32_t* a_rowsum,
+                                         void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(dtype == DSV4_BF16 || dtype == DSV4_F16, "a must be bf16 or fp16 (dtype %d)", dtype);
+  DSV4_REQUIRE(m >= 0 && m < (1ll << 31), "bad m");
+  DSV4_REQUIRE(k > 0 && k % 128 == 0 && k <= 8192, "K must be a multiple of 128 in [128, 8192]");
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(a && a_cm && a_scale && a_rowsum, "null pointer argument");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a_cm) & 7) == 0,
+               "a must be 16-byte and a_cm 8-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const bool wide = k > 2048;
+  const int rows_per_cta = wide ? 2 : 8;
+  const dim3 g(static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta));
+#define DSV4_QC(T, RT)                                                                         \
+  quant_rows_reg_kernel<T, RT, 8><<<g, 256, 0, st>>>(static_cast<const T*>(a), m, k, k, 0.f, a_cm, \
+                                                     a_scale, nullptr, nullptr, 0, m, a_rowsum)
+  if (dtype == DSV4_BF16) {
+    if (wide) DSV4_QC(__nv_bfloat16, 128); else DSV4_QC(__nv_bfloat16, 32);
+  } else {
+    if (wide) DSV4_QC(__half, 128); else DSV4_QC(__half, 32);
+  }
+#undef DSV4_QC
+  return check_launch("quant_rows_reg_kernel (K-chunk-major)");
+}
+
+int dsv4_b200_rows_to_cm(const int8_t* a_q, int64_t m, int64_t k, int64_t lda, int8_t* a_cm,
+                         int32_t* a_rowsum, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0 && m < (1ll << 31) && k > 0 && k % 128 == 0 && lda >= k && lda % 16 == 0,
+               "bad shape m=%lld k=%lld lda=%lld", (long long)m, (long long)k, (long long)lda);
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(a_q && a_cm && a_rowsum, "null pointer argument");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a_q) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a_cm) & 15) == 0,
+               "a_q and a_cm must be 16-byte aligned");
+  const int64_t blocks = (m + 7) / 8 < 4096 ? (m + 7) / 8 : 4096;
+  // identity permutation: a_scale is not copied (the caller's stays valid)
+  sort_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+      a_q, nullptr, m, k, lda, 1, nullptr, nullptr, m, 1, 1, static_cast<int>(m), a_cm, nullptr,
+      a_rowsum);
+  return check_launch("sort_rows_kernel (identity)");
+}
+
+int dsv4_b200_mxfp4_int8_dense_gemm_cm(const int8_t* a_cm, const float* a_scale,
+                                       const int32_t* a_rowsum, int64_t m, int64_t k,
+                                       const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                       int64_t shift_stride, const float* b_channel_scale,
+                                       int64_t n, void* out, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(m >= 0 && m <= 0x7FFFFFFF, "bad m");
+  if (m == 0) return DSV4_OK;
+  DSV4_REQUIRE(a_cm && a_scale && a_rowsum && b_mxfp4 && b_shift2 && b_channel_scale && out,
+               "null pointer argument");
+  return dense_common(a_cm, a_scale, m, k, b_mxfp4, b_shift2, shift_stride, b_channel_scale, n,
+                      out, nullptr, 1, n, 0, kEpiBf16, stream, a_rowsum);
 }
 
 // Allocation-free variant of dsv4_b200_mxfp4_int8_dense_gemm: the split-K

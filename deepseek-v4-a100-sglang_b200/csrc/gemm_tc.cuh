@@ -205,6 +205,14 @@ struct TcGemmCfg {
 
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 
+// SwiGLU tiles hold gate rows 0..63 and up rows 64..127 (channels j0..j0+63
+// of each).  TMEM lane 32*quarter + lane carries gate row 16*quarter + lane
+// (lane < 16) or up row 64 + 16*quarter + (lane - 16): the gate and up of a
+// channel sit 16 lanes apart in the same warp.
+__device__ __forceinline__ int swiglu_tile_row(int quarter, int lane) {
+  return (lane < 16 ? 0 : 48) + 16 * quarter + lane;
+}
+
 struct Item {
   int b, y, z;
   int expert;
@@ -592,9 +600,13 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     const int eh = (warp - 4) >> 2;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     const int row_local = quarter * 32 + lane;
-    const int e = row_local;       // 0..127 within the group
-    const int ebar = eh == 0 ? 1 : 3;  // named barrier of the group (2 is the gather warps')
-    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffStg) + eh * (16 * 128);
+    // weight row (within the tile) held in this thread's TMEM lane: SwiGLU
+    // tiles put the gate and up rows of a channel in one warp
+    // (swiglu_tile_row), so the pairing is a shuffle
+    const int wrow = EPI == kEpiSwiglu ? swiglu_tile_row(quarter, lane) : row_local;
+    // this warp's private staging slice (1 KB): the transpose of a 16-token
+    // chunk goes through it with __syncwarp only, no barrier between warps
+    uint16_t* stw = reinterpret_cast<uint16_t*>(smem + C::kOffStg + (warp - 4) * 1024);
     const float lim = p.has_clamp ? __bfloat162float(f2bf(p.clamp_limit)) : 0.f;
     uint32_t t = 0, g = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
@@ -616,7 +628,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       uint32_t accmask = 0;
       for (int q = 0; q < min(nks, C::kIssuers); ++q) accmask |= 1u << ((g + q) % C::kIssuers);
       const uint32_t t0 = tmem + (as * C::kIssuers) * C::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-      const float csn = EPI == kEpiI32 ? 0.f : meta_cs(ms)[row_local];
+      const float csn = EPI == kEpiI32 ? 0.f : meta_cs(ms)[wrow];
       // One accumulator (kIssuers == 1, the 256-token tiles): the TMEM load of
       // the next 16 columns is issued before this chunk is processed, so its
       // latency overlaps the chunk's work.
@@ -662,11 +674,10 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         if (C::kIssuers == 1 && c0 + 16 * EH >= n_mma) release_acc();
       };
 
-      // bf16((f32(acc) * a_scale) * cs) of the 16 tokens into the staging
-      // tile [token][128 rows]: scales by vector loads, rounding two values
-      // per conversion (the same round-to-nearest-even per value)
-      auto stage16 = [&](int c0, const int32_t (&v)[16]) {
-        uint16_t* sbs = reinterpret_cast<uint16_t*>(stg);
+      // bf16((f32(acc) * a_scale) * cs) of the 16 tokens of a chunk, in the
+      // reference order, two values rounded per conversion (the same
+      // round-to-nearest-even per value)
+      auto scale16 = [&](int c0, const int32_t (&v)[16], uint32_t (&pk)[8]) {
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const float4 a = reinterpret_cast<const float4*>(asc_s + c0)[q4];
@@ -676,54 +687,65 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           const float x3 = __fmul_rn(__fmul_rn(__int2float_rn(v[4 * q4 + 3]), a.w), csn);
           const __nv_bfloat162 p01 = __floats2bfloat162_rn(x0, x1);
           const __nv_bfloat162 p23 = __floats2bfloat162_rn(x2, x3);
-          const uint32_t u01 = *reinterpret_cast<const uint32_t*>(&p01);
-          const uint32_t u23 = *reinterpret_cast<const uint32_t*>(&p23);
-          sbs[(4 * q4) * 128 + row_local] = static_cast<uint16_t>(u01);
-          sbs[(4 * q4 + 1) * 128 + row_local] = static_cast<uint16_t>(u01 >> 16);
-          sbs[(4 * q4 + 2) * 128 + row_local] = static_cast<uint16_t>(u23);
-          sbs[(4 * q4 + 3) * 128 + row_local] = static_cast<uint16_t>(u23 >> 16);
+          pk[2 * q4] = *reinterpret_cast<const uint32_t*>(&p01);
+          pk[2 * q4 + 1] = *reinterpret_cast<const uint32_t*>(&p23);
         }
       };
 
       if (EPI == kEpiSwiglu) {
+        // lanes 0..15: gate of channels j0 + 16*quarter + (lane & 15); lanes
+        // 16..31: up of the same channels.  Gate lanes finish tokens 0..7,
+        // up lanes tokens 8..15, after swapping the other half by shuffle.
         const int j0 = it.y * 64;
+        const bool is_gate = lane < 16;
+        const int chl = lane & 15;
         for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
           int32_t v[16];
           load16(c0, v);
-          stage16(c0, v);
-          named_bar_sync(ebar, 128);
-          const int col = c0 + (e >> 3);
-          const int i0 = (e & 7) * 8;
-          const int orow = orow_s[col];
-          if (orow >= 0) {
-            // 8 gate and 8 up values of token col, rows i0 .. i0+7 (16-byte reads)
-            const uint4 gq = *reinterpret_cast<const uint4*>(stg + (e >> 3) * 128 + i0);
-            const uint4 uq = *reinterpret_cast<const uint4*>(stg + (e >> 3) * 128 + 64 + i0);
-            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gq);
-            const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uq);
-            uint4 hq;
-            uint32_t* h2 = reinterpret_cast<uint32_t*>(&hq);
+          uint32_t pk[8];
+          scale16(c0, v, pk);
+          // own bf16 pairs: tokens (2p, 2p+1) in pk[p]
+          uint32_t mine[4], other[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {  // two rows per step, rounded as a pair
-              float2 gv = __bfloat1622float2(g2[u]);
-              float2 up = __bfloat1622float2(u2[u]);
-              if (p.has_clamp) {
-                gv.x = fminf(gv.x, lim), gv.y = fminf(gv.y, lim);
-                up.x = fminf(fmaxf(up.x, -lim), lim), up.y = fminf(fmaxf(up.y, -lim), lim);
-              }
-              // silu in fast fp32 (MUFU exp2 / reciprocal): the result is
-              // rounded to bf16, where it differs from the IEEE-exact form by
-              // at most one ulp, and rarely
-              const float2 sg = __bfloat1622float2(
-                  __floats2bfloat162_rn(__fdividef(gv.x, 1.0f + __expf(-gv.x)),
-                                        __fdividef(gv.y, 1.0f + __expf(-gv.y))));
-              const __nv_bfloat162 hh =
-                  __floats2bfloat162_rn(__fmul_rn(sg.x, up.x), __fmul_rn(sg.y, up.y));
-              h2[u] = *reinterpret_cast<const uint32_t*>(&hh);
-            }
-            *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo + j0 + i0) = hq;
+          for (int pp = 0; pp < 4; ++pp) {
+            const uint32_t send = is_gate ? pk[4 + pp] : pk[pp];  // gate: tokens 8..15, up: 0..7
+            other[pp] = __shfl_xor_sync(0xffffffffu, send, 16);
+            mine[pp] = is_gate ? pk[pp] : pk[4 + pp];
           }
-          named_bar_sync(ebar, 128);
+          const int tok0 = is_gate ? 0 : 8;
+#pragma unroll
+          for (int pp = 0; pp < 4; ++pp) {
+            const uint32_t gw = is_gate ? mine[pp] : other[pp];
+            const uint32_t uw = is_gate ? other[pp] : mine[pp];
+            float2 gv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw));
+            float2 up = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw));
+            if (p.has_clamp) {
+              gv.x = fminf(gv.x, lim), gv.y = fminf(gv.y, lim);
+              up.x = fminf(fmaxf(up.x, -lim), lim), up.y = fminf(fmaxf(up.y, -lim), lim);
+            }
+            // silu in fast fp32 (MUFU exp2 / reciprocal): the result is
+            // rounded to bf16, where it differs from the IEEE-exact form by
+            // at most one ulp, and rarely
+            const float2 sg = __bfloat1622float2(
+                __floats2bfloat162_rn(__fdividef(gv.x, 1.0f + __expf(-gv.x)),
+                                      __fdividef(gv.y, 1.0f + __expf(-gv.y))));
+            const __nv_bfloat162 hh =
+                __floats2bfloat162_rn(__fmul_rn(sg.x, up.x), __fmul_rn(sg.y, up.y));
+            const uint32_t hw = *reinterpret_cast<const uint32_t*>(&hh);
+            // staging [16 tokens][16 channels] bf16
+            stw[(tok0 + 2 * pp) * 16 + chl] = static_cast<uint16_t>(hw);
+            stw[(tok0 + 2 * pp + 1) * 16 + chl] = static_cast<uint16_t>(hw >> 16);
+          }
+          __syncwarp();
+          {
+            const int tok = lane >> 1, half = lane & 1;
+            const int orow = orow_s[c0 + tok];
+            const uint4 hq = *reinterpret_cast<const uint4*>(stw + tok * 16 + 8 * half);
+            if (orow >= 0)
+              *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo + j0 +
+                                        16 * quarter + 8 * half) = hq;
+          }
+          __syncwarp();
         }
       } else {
         const int n_g = it.y * 128 + row_local;
@@ -731,22 +753,29 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           int32_t v[16];
           load16(c0, v);
           if (EPI == kEpiBf16) {
-            // staged through shared memory ([token][128 channels] bf16) so a
-            // thread stores 32 contiguous bytes of one token row instead of
-            // 16 scattered 2-byte values
-            stage16(c0, v);
-            named_bar_sync(ebar, 128);
-            const int col = e >> 3;         // token of the chunk
-            const int ch0 = (e & 7) * 16;   // 16 channels
-            const int orow = orow_s[c0 + col];
-            if (orow >= 0) {
-              const uint4* src = reinterpret_cast<const uint4*>(stg + col * 128 + ch0);
-              uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo +
-                                                    it.y * 128 + ch0);
-              dst[0] = src[0];
-              dst[1] = src[1];
+            // transpose through the warp's staging slice [16 tokens][32
+            // channels]: lane 8a + i then stores channels 8a..8a+7 of tokens
+            // i and 8 + i as two 16-byte stores (each token row of the warp
+            // is 64 contiguous bytes)
+            uint32_t pk[8];
+            scale16(c0, v, pk);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              stw[(2 * q) * 32 + lane] = static_cast<uint16_t>(pk[q]);
+              stw[(2 * q + 1) * 32 + lane] = static_cast<uint16_t>(pk[q] >> 16);
             }
-            named_bar_sync(ebar, 128);
+            __syncwarp();
+            const int i = lane & 7, a8 = (lane >> 3) * 8;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int tok = 8 * h + i;
+              const int orow = orow_s[c0 + tok];
+              const uint4 val = *reinterpret_cast<const uint4*>(stw + tok * 32 + a8);
+              if (orow >= 0)
+                *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo +
+                                          it.y * 128 + quarter * 32 + a8) = val;
+            }
+            __syncwarp();
           } else {
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
@@ -775,7 +804,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     // (64 TMEM columns: block kb -> columns 8kb .. 8kb+7).
     const int quarter = warp & 3;
     const int grp = (warp - C::kDecBase) >> 2;
-    const int row = quarter * 32 + lane;
+    // weight row of the tile decoded into this thread's TMEM lane
+    const int row = EPI == kEpiSwiglu ? swiglu_tile_row(quarter, lane) : quarter * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16, one = p.dec_one;
     uint32_t g = 0, cc = 0;

@@ -4,6 +4,8 @@
 // reduce.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace dsv4 {
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
     const int idx = lt + i * RT;
     if (active && idx < nv) {
       // 8 elements at k = 8 idx; K-chunk-major: chunk idx / 16, byte 8 (idx % 16)
-      uint2* dst = sorted == nullptr
+      uint2* dst = cm_rows == 0
                        ? qr + idx
                        : reinterpret_cast<uint2*>(q + (idx >> 4) * cm_rows * 128 + row * 128 + (idx & 15) * 8);
       const T* e = reinterpret_cast<const T*>(&u[i]);
@@ -183,8 +185,10 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
 // rows are slots) of a_q and its scale, K-chunk-major [K/128][cap][128].
 // Padding positions are left unwritten (their MMA columns are never stored).
 // Source rows are lda bytes apart and their scales scale_stride floats apart
-// (rows received packed with their metadata).  One warp per position, 16 B
-// per lane.
+// (rows received packed with their metadata).  With sorted == nullptr the
+// permutation is the identity over cap positions (dense activations into the
+// K-chunk-major layout; out_scale may then be null).  One warp per position,
+// 16 B per lane.
 __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict__ a,
                                                         const float* __restrict__ a_scale,
                                                         int64_t a_rows, int64_t k,
@@ -196,14 +200,15 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
                                                         float* __restrict__ out_scale,
                                                         int32_t* __restrict__ out_rowsum) {
   const int lane = threadIdx.x & 31;
-  const int64_t n = min(cap, static_cast<int64_t>(__ldg(ntpp)));
+  const int64_t n = ntpp != nullptr ? min(cap, static_cast<int64_t>(__ldg(ntpp))) : cap;
   const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int nv = static_cast<int>(k / 16);
   for (int64_t pos = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; pos < n;
        pos += nw) {
-    const int slot = __ldg(sorted + pos);
+    // no permutation (sorted == nullptr): position p holds row p
+    const int slot = sorted != nullptr ? __ldg(sorted + pos) : static_cast<int>(pos);
     if (slot < 0 || slot >= num_valid) continue;
-    const int64_t src = src_is_slot ? slot : slot / topk;
+    const int64_t src = sorted == nullptr || src_is_slot ? slot : slot / topk;
     if (src >= a_rows) continue;
     const int4* row = reinterpret_cast<const int4*>(a + src * lda);
     int sum = 0;
@@ -215,7 +220,7 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (lane == 0) {
-      out_scale[pos] = __ldg(a_scale + src * scale_stride);
+      if (out_scale != nullptr) out_scale[pos] = __ldg(a_scale + src * scale_stride);
       out_rowsum[pos] = sum;
     }
   }
@@ -228,15 +233,13 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
 // renormalised to sum 1 when asked, times `scale`.  One warp per token, EPL
 // experts per lane in registers; k rounds of a warp argmax (ties: lower
 // expert index), so the k results come out in descending order.
+// One token's routing by one warp; lanes r < topk end with (my_id, my_w) of
+// the r-th choice.
 template <typename T, int EPL>
-__global__ void __launch_bounds__(256) router_topk_kernel(const T* __restrict__ logits, int64_t m,
-                                                          int e, const float* __restrict__ bias,
-                                                          int topk, int renormalize, float scale,
-                                                          int32_t* __restrict__ ids,
-                                                          float* __restrict__ weights) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (row >= m) return;
+__device__ __forceinline__ void router_row(const T* __restrict__ logits, int64_t row, int e,
+                                           const float* __restrict__ bias, int topk,
+                                           int renormalize, float scale, int lane, int& out_id,
+                                           float& out_w) {
   float sel[EPL], sc[EPL];
 #pragma unroll
   for (int j = 0; j < EPL; ++j) {
@@ -277,10 +280,25 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const T* __restrict__ 
     wsum += w;
     if (lane == r) my_w = w, my_id = bx;
   }
+  out_id = my_id;
+  out_w = (renormalize ? my_w / wsum : my_w) * scale;
+}
+
+template <typename T, int EPL>
+__global__ void __launch_bounds__(256) router_topk_kernel(const T* __restrict__ logits, int64_t m,
+                                                          int e, const float* __restrict__ bias,
+                                                          int topk, int renormalize, float scale,
+                                                          int32_t* __restrict__ ids,
+                                                          float* __restrict__ weights) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= m) return;
+  int id;
+  float w;
+  router_row<T, EPL>(logits, row, e, bias, topk, renormalize, scale, lane, id, w);
   if (lane < topk) {
-    const float w = renormalize ? my_w / wsum : my_w;
-    ids[row * topk + lane] = my_id;
-    weights[row * topk + lane] = w * scale;
+    ids[row * topk + lane] = id;
+    weights[row * topk + lane] = w;
   }
 }
 
@@ -679,6 +697,140 @@ ep_plan_fixed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ 
       run[t0] += tot;
     }
     __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// f2. Router top-k fused with the expert align: one cooperative launch from
+// router logits to (topk_ids, topk_weights, sorted_token_ids, expert_ids,
+// num_tokens_post_padded).  Same results, bit for bit, as router_topk_kernel
+// followed by moe_align_kernel (stable order: increasing slot id inside each
+// expert; padding value m*topk).  CTA c owns tokens [c*tpc, (c+1)*tpc) and its
+// warps own contiguous sub-ranges, so slot order = (CTA, warp, token, k).
+//   phase 1  route each token (router_row), count per (warp, expert) in
+//            shared memory, publish per-(CTA, expert) totals; fill padding
+//   grid sync
+//   phase 2  per expert: CTA base (earlier CTAs' totals) and the
+//            block-padded exclusive prefix over experts (every CTA computes
+//            it); expert_ids / ntpp written grid-stride
+//   phase 3  each warp places its slots
+// Shared memory: wc [32][E] + cbase [E] + ebase [E + 1] + scan [32] ints.
+// ---------------------------------------------------------------------------
+constexpr int kRouteAlignThreads = 1024;
+
+__host__ __device__ constexpr int route_align_smem_bytes(int experts) {
+  return (32 * experts + experts + experts + 1 + 32) * 4;
+}
+
+template <typename T, int EPL>
+__global__ void __launch_bounds__(kRouteAlignThreads, 1)
+router_align_kernel(const T* __restrict__ logits, int m, int num_experts,
+                    const float* __restrict__ bias, int topk, int renormalize, float scale,
+                    int block_m, int tpc, int32_t* __restrict__ topk_ids,
+                    float* __restrict__ topk_weights, int32_t* __restrict__ sorted_ids,
+                    int sorted_cap, int32_t* __restrict__ expert_ids, int expert_cap,
+                    int32_t* __restrict__ ntpp, int32_t* __restrict__ cta_counts) {
+  extern __shared__ int sm_ra[];
+  const int E = num_experts;
+  int* wc = sm_ra;             // [32][E] per-warp counts, then per-warp cursors
+  int* cbase = wc + 32 * E;    // [E] this CTA's base inside each expert
+  int* ebase = cbase + E;      // [E + 1] padded exclusive prefix over experts
+  int* scan = ebase + E + 1;   // [32]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x, G = gridDim.x;
+  const int t_begin = min(m, c * tpc), t_end = min(m, t_begin + tpc);
+  const int tpw = (tpc + 31) / 32;
+  const int w_begin = min(t_end, t_begin + warp * tpw), w_end = min(t_end, w_begin + tpw);
+  const int numel = m * topk;
+
+  for (int i = tid; i < 32 * E; i += kRouteAlignThreads) wc[i] = 0;
+  for (int i = c * kRouteAlignThreads + tid; i < sorted_cap; i += G * kRouteAlignThreads)
+    sorted_ids[i] = numel;
+  __syncthreads();
+  // phase 1: route, count
+  for (int t = w_begin; t < w_end; ++t) {
+    int id;
+    float w;
+    router_row<T, EPL>(logits, t, E, bias, topk, renormalize, scale, lane, id, w);
+    if (lane < topk) {
+      topk_ids[static_cast<int64_t>(t) * topk + lane] = id;
+      topk_weights[static_cast<int64_t>(t) * topk + lane] = w;
+      wc[warp * E + id] += 1;  // a token's experts are distinct: no two lanes collide
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kRouteAlignThreads) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int v = wc[w * E + e];
+      wc[w * E + e] = run;
+      run += v;
+    }
+    cta_counts[static_cast<int64_t>(c) * E + e] = run;
+  }
+  cooperative_groups::this_grid().sync();
+  // phase 2: bases
+  int cnt = 0;
+  if (tid < E) {
+    int before = 0, total = 0;
+    for (int q = 0; q < G; ++q) {
+      const int v = __ldcg(cta_counts + static_cast<int64_t>(q) * E + tid);
+      if (q < c) before += v;
+      total += v;
+    }
+    cbase[tid] = before;
+    cnt = total;
+  }
+  {
+    const int padded = (cnt + block_m - 1) / block_m * block_m;
+    int v = padded;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) scan[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int w = scan[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      scan[lane] = w;
+    }
+    __syncthreads();
+    const int incl = v + (warp > 0 ? scan[warp - 1] : 0);
+    if (tid < E) ebase[tid] = incl - padded;
+    if (tid == E - 1) ebase[E] = incl;
+  }
+  __syncthreads();
+  const int total = ebase[E];
+  for (int b = c * kRouteAlignThreads + tid; b < expert_cap; b += G * kRouteAlignThreads) {
+    int e = -1;
+    const int pos = b * block_m;
+    if (pos < total) {
+      int lo = 0, hi = E - 1;  // last e with ebase[e] <= pos
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (ebase[mid] <= pos) lo = mid; else hi = mid - 1;
+      }
+      e = lo;
+    }
+    expert_ids[b] = e;
+  }
+  if (c == 0 && tid == 0) ntpp[0] = total;
+  // phase 3: place this warp's slots in (token, k) order
+  for (int t = w_begin; t < w_end; ++t) {
+    if (lane < topk) {
+      const int e = topk_ids[static_cast<int64_t>(t) * topk + lane];
+      const int pos = ebase[e] + cbase[e] + wc[warp * E + e];
+      if (pos < sorted_cap) sorted_ids[pos] = t * topk + lane;
+      wc[warp * E + e] += 1;
+    }
+    __syncwarp();
   }
 }
 

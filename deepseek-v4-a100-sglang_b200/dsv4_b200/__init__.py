@@ -18,6 +18,8 @@ from .mxfp4_int8_moe import (  # noqa: F401
     select_mxfp4_int8_moe_tile_shape,
     select_sorted_block_m,
     router_topk,
+    router_align,
+    mxfp4_int8_moe_forward_from_logits,
 )
 from .jit_ops import (  # noqa: F401
     mxfp4_int8_dense_gemm,

@@ -33,6 +33,9 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_get_device_status": [_P, _I],
     "dsv4_b200_quantize_per_token_int8": [_P, _I, _I64, _I64, _I64, _F, _P, _P, _P],
     "dsv4_b200_remap_mxfp4_weight_for_int8": [_P, _P, _I64, _I64, _I64, _I, _I, _P, _P, _P, _P],
+    "dsv4_b200_router_align_workspace_words": [_I64, _I64, _P],
+    "dsv4_b200_router_align": [_P, _I, _I64, _I64, _P, _I64, _I, _F, _I64, _P, _P, _P, _I64, _P,
+                               _I64, _P, _P, _I64, _P],
     "dsv4_b200_moe_align_block_size": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P],
     "dsv4_b200_mxfp4_int8_moe_gemm": [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P,
                                       _I64, _P, _I64, _P, _I64, _I64, _I, _I64, _P],
@@ -57,6 +60,10 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_mxfp4_int8_dense_gemm": [_P, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _P,
                                         _I64, _I64, _P],
     "dsv4_b200_mxfp4_int8_dense_gemm_i32": [_P, _I64, _I64, _P, _P, _I64, _I64, _P, _P],
+    "dsv4_b200_quantize_per_token_int8_cm": [_P, _I, _I64, _I64, _P, _P, _P, _P],
+    "dsv4_b200_rows_to_cm": [_P, _I64, _I64, _I64, _P, _P, _P],
+    "dsv4_b200_mxfp4_int8_dense_gemm_cm": [_P, _P, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P,
+                                           _P],
     "dsv4_b200_mxfp4_int8_dense_gemm_noalloc": [_P, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P,
                                                 _P],
 }

@@ -325,10 +325,59 @@ def mxfp4_int8_dense_gemm(a_q, a_scale, b_mxfp4, b_shift2, b_channel_scale, out,
         _check(partial.dim() == 3 and partial.shape[1] == m and partial.shape[2] == acc_ld,
                f"partial must be [splits, {m}, {acc_ld}], got {tuple(partial.shape)}")
     _init_device(dev)
+    if use_cm_tile(m, k, n):
+        a_cm, rs = rows_to_cm(a_q)
+        dense_gemm_cm(a_cm, a_scale, rs, b_mxfp4, b_shift2, b_channel_scale, out)
+        return
     N.call("dsv4_b200_mxfp4_int8_dense_gemm", a_q.data_ptr(), a_scale.data_ptr(), m, k,
            b_mxfp4.data_ptr(), b_shift2.data_ptr(), b_shift2.shape[0], b_channel_scale.data_ptr(),
            n, out.data_ptr(), partial.data_ptr() if use_partial else None,
            partial.shape[0] if use_partial else 0, acc_ld, N.stream_of(a_q))
+
+
+def use_cm_tile(m: int, k: int, n: int) -> bool:
+    """Large M runs on the 256-token K-chunk-major tile (above
+    ``DSV4_B200_DENSE_CM_MIN_M`` rows, default 128)."""
+    import os
+    lim = int(os.environ.get("DSV4_B200_DENSE_CM_MIN_M", "128"))
+    return m > lim and k % 128 == 0 and n % 128 == 0
+
+
+def rows_to_cm(a_q):
+    """Row-major int8 [M, K] -> (K-chunk-major int8 [K/128 * M * 128], int32 row sums [M])."""
+    m, k = a_q.shape
+    a_cm = torch.empty(m * k, device=a_q.device, dtype=torch.int8)
+    rs = torch.empty(m, device=a_q.device, dtype=torch.int32)
+    N.call("dsv4_b200_rows_to_cm", a_q.data_ptr(), m, k, a_q.stride(0), a_cm.data_ptr(),
+           rs.data_ptr(), N.stream_of(a_q))
+    return a_cm, rs
+
+
+def quantize_per_token_int8_cm(a):
+    """Per-token INT8 quantisation of bf16/fp16 ``a`` [M, K] straight into the
+    K-chunk-major layout: ``(a_cm, scale [M], rowsum [M])``."""
+    _check(a.dim() == 2 and a.dtype in (torch.bfloat16, torch.float16) and a.is_contiguous(),
+           "a must be a contiguous 2-D bf16/fp16 tensor")
+    m, k = a.shape
+    a_cm = torch.empty(m * k, device=a.device, dtype=torch.int8)
+    sc = torch.empty(m, device=a.device, dtype=torch.float32)
+    rs = torch.empty(m, device=a.device, dtype=torch.int32)
+    _init_device(a.device)
+    N.call("dsv4_b200_quantize_per_token_int8_cm", a.data_ptr(),
+           N.DTYPE_BF16 if a.dtype == torch.bfloat16 else N.DTYPE_F16, m, k, a_cm.data_ptr(),
+           sc.data_ptr(), rs.data_ptr(), N.stream_of(a))
+    return a_cm, sc, rs
+
+
+def dense_gemm_cm(a_cm, a_scale, a_rowsum, b_mxfp4, b_shift2, b_channel_scale, out) -> None:
+    """Dense GEMM on K-chunk-major activations (256-token tiles)."""
+    m = a_scale.shape[0]
+    n = b_channel_scale.shape[0]
+    k = b_mxfp4.shape[0] * 32
+    _check_tensor(out, "out", torch.bfloat16, (m, n), a_scale.device)
+    N.call("dsv4_b200_mxfp4_int8_dense_gemm_cm", a_cm.data_ptr(), a_scale.data_ptr(),
+           a_rowsum.data_ptr(), m, k, b_mxfp4.data_ptr(), b_shift2.data_ptr(), b_shift2.shape[0],
+           b_channel_scale.data_ptr(), n, out.data_ptr(), N.stream_of(out))
 
 
 def mxfp4_int8_dense_gemm_i32(a_q, b_mxfp4, b_shift2, n: int) -> torch.Tensor:

@@ -26,6 +26,9 @@ from .jit_ops import (
     quantize_sorted_int8,
     mxfp4_int8_moe_gemm_swiglu_sorted,
     mxfp4_int8_moe_gemm_sorted,
+    use_cm_tile,
+    quantize_per_token_int8_cm,
+    dense_gemm_cm,
 )
 
 _VALID_BLOCK_M = {16, 32, 64, 128}
@@ -143,10 +146,19 @@ def mxfp4_int8_dense_forward(hidden_states: torch.Tensor, weight: Mxfp4Int8Dense
     if bias is not None:
         raise NotImplementedError("MXFP4-int8 dense JIT path does not support bias")
     hidden_states = hidden_states.contiguous()
-    a_q, a_scale = quantize_per_token_int8(hidden_states, 0.0)
     n = weight.weight_channel_scale.shape[0]
-    m = hidden_states.shape[0]
+    m, k = hidden_states.shape
     out = torch.empty((m, n), device=hidden_states.device, dtype=torch.bfloat16)
+    if (use_cm_tile(m, k, n) and hidden_states.dtype in (torch.bfloat16, torch.float16)
+            and k <= 8192):
+        # large M: quantise straight into the K-chunk-major layout of the
+        # 256-token tile (same numbers as the row-major quantiser)
+        _require_cuda(hidden_states, "hidden_states")
+        a_cm, a_scale, rs = quantize_per_token_int8_cm(hidden_states)
+        dense_gemm_cm(a_cm, a_scale, rs, weight.weight_mxfp4, weight.weight_shift2,
+                      weight.weight_channel_scale, out)
+        return out
+    a_q, a_scale = quantize_per_token_int8(hidden_states, 0.0)
     partial = (torch.empty((4, m, (n + 31) // 32 * 32), device=hidden_states.device, dtype=torch.int32)
                if m <= 128 else torch.empty((0,), device=hidden_states.device, dtype=torch.int32))
     mxfp4_int8_dense_gemm(a_q, a_scale, weight.weight_mxfp4, weight.weight_shift2,
@@ -252,6 +264,43 @@ def router_topk(router_logits: torch.Tensor, topk: int, *, bias: torch.Tensor | 
     return ids, w
 
 
+def router_align(router_logits: torch.Tensor, topk: int, block_size: int, *,
+                 bias: torch.Tensor | None = None, renormalize: bool = True,
+                 scale: float = 1.0):
+    """:func:`router_topk` and :func:`moe_align_block_size` in one launch
+    (a cooperative kernel; same results bit for bit).  Returns
+    ``(topk_ids, topk_weights, sorted_token_ids, expert_ids,
+    num_tokens_post_pad)``."""
+    if router_logits.dim() != 2 or router_logits.dtype not in _DTYPES:
+        raise ValueError("router_logits must be a 2-D fp32/fp16/bf16 tensor")
+    _require_cuda(router_logits, "router_logits")
+    logits = router_logits.contiguous()
+    m, e = logits.shape
+    dev = logits.device
+    b = None
+    if bias is not None:
+        b = bias.to(device=dev, dtype=torch.float32).contiguous()
+        if b.shape != (e,):
+            raise ValueError(f"bias must have shape [{e}], got {tuple(b.shape)}")
+    ids = torch.empty((m, topk), device=dev, dtype=torch.int32)
+    w = torch.empty((m, topk), device=dev, dtype=torch.float32)
+    cap = align_capacity(m * topk, e, block_size)
+    sorted_ids = torch.empty((cap,), dtype=torch.int32, device=dev)
+    n_blocks = (cap + block_size - 1) // block_size
+    expert_ids = torch.empty((n_blocks,), dtype=torch.int32, device=dev)
+    ntpp = torch.empty((1,), dtype=torch.int32, device=dev)
+    import ctypes
+    words = ctypes.c_int64(0)
+    N.call("dsv4_b200_router_align_workspace_words", m, e, ctypes.byref(words))
+    ws = torch.empty((max(words.value, 1),), dtype=torch.int32, device=dev)
+    N.call("dsv4_b200_router_align", logits.data_ptr(), _DTYPES[logits.dtype], m, e,
+           b.data_ptr() if b is not None else None, topk, 1 if renormalize else 0, float(scale),
+           block_size, ids.data_ptr(), w.data_ptr(), sorted_ids.data_ptr(), cap,
+           expert_ids.data_ptr(), n_blocks, ntpp.data_ptr(), ws.data_ptr(), ws.numel(),
+           N.stream_of(logits))
+    return ids, w, sorted_ids, expert_ids, ntpp
+
+
 def align_capacity(numel: int, num_experts: int, block_size: int) -> int:
     """PYMOE:848-851."""
     if numel < num_experts + 1:
@@ -309,6 +358,36 @@ def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWei
                      intermediate_size=intermediate_size,
                      routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
                      masked=False)
+
+
+def mxfp4_int8_moe_forward_from_logits(hidden_states: torch.Tensor,
+                                       weights: Mxfp4Int8MoeWeights,
+                                       router_logits: torch.Tensor, topk: int, *,
+                                       hidden_size: int, intermediate_size: int,
+                                       router_bias: torch.Tensor | None = None,
+                                       renormalize: bool = True,
+                                       routed_scaling_factor: float | None = None,
+                                       clamp_limit: float | None = None):
+    """The MoE layer from router logits: routing and expert align in one fused
+    launch (:func:`router_align`), then the same launches as
+    :func:`mxfp4_int8_moe_forward`.  Returns ``(out, topk_ids, topk_weights)``."""
+    if hidden_states.dtype != torch.bfloat16:
+        hidden_states = hidden_states.to(torch.bfloat16)
+    hidden_states = hidden_states.contiguous()
+    _require_cuda(hidden_states, "hidden_states")
+    m = hidden_states.shape[0]
+    experts = weights.w13_mxfp4.shape[0]
+    _, block_n = _select_moe_tile_shape(m, topk, experts)
+    block_m = select_sorted_block_m(m, topk, experts)
+    ids, w, sorted_ids, expert_ids, ntpp = router_align(router_logits, topk, block_m,
+                                                        bias=router_bias, renormalize=renormalize)
+    a13_q, a13_scale = quantize_per_token_int8(hidden_states, 0.0)
+    out = _moe_core(a13_q, a13_scale, weights, ids, w, sorted_ids, expert_ids, ntpp,
+                    block_m=block_m, block_n=block_n, hidden_size=hidden_size,
+                    intermediate_size=intermediate_size,
+                    routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
+                    masked=False)
+    return out, ids, w
 
 
 def _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids, expert_ids,

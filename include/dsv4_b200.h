@@ -93,6 +93,27 @@ DSV4_API int dsv4_b200_router_topk(const void* logits, int dtype, int64_t m, int
                                    const float* bias, int64_t topk, int renormalize, float scale,
                                    int32_t* topk_ids, float* topk_weights, void* stream);
 
+/* Router top-k fused with the expert align (row f2; the reference gets its
+ * routing from SGLang's top-k, PATCH:505-507, then aligns with
+ * sgl_kernel.moe_align_block_size, PYMOE:842-869).  One cooperative launch
+ * computes what dsv4_b200_router_topk followed by
+ * dsv4_b200_moe_align_block_size compute, bit for bit: topk_ids /
+ * topk_weights [m][topk], sorted_token_ids (stable order, padding m*topk),
+ * expert_ids, num_tokens_post_pad.  `workspace` holds per-CTA expert counts:
+ * at least the number of int32 words that
+ * dsv4_b200_router_align_workspace_words(m, num_experts) reports; nothing in
+ * it needs to start at zero.  num_experts <= 1024. */
+DSV4_API int dsv4_b200_router_align_workspace_words(int64_t m, int64_t num_experts,
+                                                    int64_t* words);
+DSV4_API int dsv4_b200_router_align(const void* logits, int dtype, int64_t m,
+                                    int64_t num_experts, const float* bias, int64_t topk,
+                                    int renormalize, float scale, int64_t block_size,
+                                    int32_t* topk_ids, float* topk_weights,
+                                    int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                    int32_t* expert_ids, int64_t expert_ids_capacity,
+                                    int32_t* num_tokens_post_pad, int32_t* workspace,
+                                    int64_t workspace_words, void* stream);
+
 /* a5. Expert histogram + block-padded prefix sum + stable permutation.
  * Replaces the sgl_kernel.moe_align_block_size call of
  * _moe_align_block_size (PYMOE:842-869).  topk_ids int32 [numel]; experts
@@ -269,6 +290,29 @@ DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm_i32(const int8_t* a_q, int64_t m, i
                                         const uint8_t* b_mxfp4, const uint8_t* b_shift2,
                                         int64_t shift_stride, int64_t n, int32_t* acc,
                                         void* stream);
+
+/* Dense GEMM on the 256-token K-chunk-major tile (B200 fast path for large
+ * M; same results, bit for bit, as dsv4_b200_mxfp4_int8_dense_gemm, which
+ * it serves through the Python op for M > 128: reference DENSE_ENTRY:410-432
+ * is the large-M branch it replaces).  Activations are K-chunk-major int8
+ * a_cm [k/128][m][128] with per-row scales and int8 row sums (the decode is
+ * biased unsigned, corrected by 128 * rowsum).
+ * dsv4_b200_quantize_per_token_int8_cm: the per-token quantiser of
+ *   dsv4_b200_quantize_per_token_int8 (PYMOE:53-126) writing that layout
+ *   (bf16/fp16 input, k a multiple of 128, <= 8192).
+ * dsv4_b200_rows_to_cm: row-major int8 rows (lda bytes apart) into that
+ *   layout plus row sums; the scales are unchanged. */
+DSV4_API int dsv4_b200_quantize_per_token_int8_cm(const void* a, int dtype, int64_t m, int64_t k,
+                                                  int8_t* a_cm, float* a_scale, int32_t* a_rowsum,
+                                                  void* stream);
+DSV4_API int dsv4_b200_rows_to_cm(const int8_t* a_q, int64_t m, int64_t k, int64_t lda,
+                                  int8_t* a_cm, int32_t* a_rowsum, void* stream);
+DSV4_API int dsv4_b200_mxfp4_int8_dense_gemm_cm(const int8_t* a_cm, const float* a_scale,
+                                                const int32_t* a_rowsum, int64_t m, int64_t k,
+                                                const uint8_t* b_mxfp4, const uint8_t* b_shift2,
+                                                int64_t shift_stride,
+                                                const float* b_channel_scale, int64_t n,
+                                                void* out, void* stream);
 
 /* Dense MXFP4 x INT8 GEMM for callers that cannot allocate device memory.
  * No counterpart in the reference.  Same math and arguments as
