@@ -713,6 +713,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             mine[pp] = is_gate ? pk[pp] : pk[4 + pp];
           }
           const int tok0 = is_gate ? 0 : 8;
+          uint32_t hw[4];
 #pragma unroll
           for (int pp = 0; pp < 4; ++pp) {
             const uint32_t gw = is_gate ? mine[pp] : other[pp];
@@ -731,10 +732,37 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
                                       __fdividef(gv.y, 1.0f + __expf(-gv.y))));
             const __nv_bfloat162 hh =
                 __floats2bfloat162_rn(__fmul_rn(sg.x, up.x), __fmul_rn(sg.y, up.y));
-            const uint32_t hw = *reinterpret_cast<const uint32_t*>(&hh);
-            // staging [16 tokens][16 channels] bf16
-            stw[(tok0 + 2 * pp) * 16 + chl] = static_cast<uint16_t>(hw);
-            stw[(tok0 + 2 * pp + 1) * 16 + chl] = static_cast<uint16_t>(hw >> 16);
+            hw[pp] = *reinterpret_cast<const uint32_t*>(&hh);
+          }
+          // staging [16 tokens][16 channels] bf16 as 32-bit words of two
+          // channels: lanes (2j, 2j+1) of a half swap token halves by
+          // shuffle; the even lane writes tokens tok0 + 0..3, the odd lane
+          // tok0 + 4..7 of channels (2j, 2j+1), each of the four lane groups
+          // starting at a different row so one store spans all banks
+          {
+            const uint32_t odd = chl & 1;
+            const uint32_t r0 = __shfl_xor_sync(0xffffffffu, odd ? hw[0] : hw[2], 1);
+            const uint32_t r1 = __shfl_xor_sync(0xffffffffu, odd ? hw[1] : hw[3], 1);
+            const uint32_t o0 = odd ? hw[2] : hw[0], o1 = odd ? hw[3] : hw[1];
+            const uint32_t e0 = odd ? r0 : o0, d0 = odd ? o0 : r0;
+            const uint32_t e1 = odd ? r1 : o1, d1 = odd ? o1 : r1;
+            uint32_t wv4[4];
+            wv4[0] = (e0 & 0xFFFFu) | (d0 << 16);
+            wv4[1] = (e0 >> 16) | (d0 & 0xFFFF0000u);
+            wv4[2] = (e1 & 0xFFFFu) | (d1 << 16);
+            wv4[3] = (e1 >> 16) | (d1 & 0xFFFF0000u);
+            const int tb = tok0 + (odd ? 4 : 0);
+            const int gidx = (lane >> 4) * 2 + static_cast<int>(odd);
+            uint32_t* s32 = reinterpret_cast<uint32_t*>(stw);
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+              const int xx = (x + gidx) & 3;
+              uint32_t val = wv4[0];
+              val = xx == 1 ? wv4[1] : val;
+              val = xx == 2 ? wv4[2] : val;
+              val = xx == 3 ? wv4[3] : val;
+              s32[(tb + xx) * 8 + (chl >> 1)] = val;
+            }
           }
           __syncwarp();
           {
@@ -759,10 +787,25 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             // is 64 contiguous bytes)
             uint32_t pk[8];
             scale16(c0, v, pk);
+            // 32-bit words of two neighbouring channels: lane pairs (2j, 2j+1)
+            // swap halves by shuffle, the even lane then writes tokens 0..7
+            // and the odd lane tokens 8..15 of channels (2j, 2j+1); rows of
+            // opposite parity in one store keep the two lane sets on
+            // different banks (2-byte stores put two lanes on one word)
+            {
+              const uint32_t odd = lane & 1;
+              const int tb = odd ? 8 : 0, j = lane >> 1;
+              uint32_t* s32 = reinterpret_cast<uint32_t*>(stw);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              stw[(2 * q) * 32 + lane] = static_cast<uint16_t>(pk[q]);
-              stw[(2 * q + 1) * 32 + lane] = static_cast<uint16_t>(pk[q] >> 16);
+              for (int qq = 0; qq < 4; ++qq) {
+                const uint32_t par = __shfl_xor_sync(0xffffffffu, odd ? pk[qq] : pk[4 + qq], 1);
+                const uint32_t own = odd ? pk[4 + qq] : pk[qq];
+                const uint32_t ev = odd ? par : own, od = odd ? own : par;
+                const uint32_t w0 = (ev & 0xFFFFu) | (od << 16);          // token tb + 2qq
+                const uint32_t w1 = (ev >> 16) | (od & 0xFFFF0000u);      // token tb + 2qq + 1
+                s32[(tb + 2 * qq + odd) * 16 + j] = odd ? w1 : w0;
+                s32[(tb + 2 * qq + 1 - odd) * 16 + j] = odd ? w0 : w1;
+              }
             }
             __syncwarp();
             const int i = lane & 7, a8 = (lane >> 3) * 8;
@@ -846,11 +889,6 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             wv[kb] = *reinterpret_cast<const uint4*>(P + poff);
           }
           (void)nkb;
-          // The packed slot is free once it is in registers: hand it back to the
-          // TMA producer now, not after the decode (the arrive has release
-          // semantics, ordering the loads above).
-          __syncwarp();
-          if (lane == 0) mbar_arrive(pk_empty(sp));
           mbar_wait(a_empty(sa), ((gs / SA) & 1) ^ 1, kErrWaitAbEmpty);
           if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, gs);
           tc_fence_after();
@@ -883,6 +921,14 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             tmem_st_x16(tcol + 16 * q, v);
 #endif
           }
+          // The packed slot goes back to the TMA producer only after the
+          // decode has consumed the loaded registers.  Handing it back right
+          // after issuing the shared-memory loads let a refill overwrite
+          // bytes a lane had not read yet (one warp's 32 weight rows of a
+          // stage decoded from the next stage's codes, seen as one corrupt
+          // TMEM quarter per item in repeated full-size runs).
+          __syncwarp();
+          if (lane == 0) mbar_arrive(pk_empty(sp));
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();

@@ -194,3 +194,45 @@ def test_dense_config1_full_shape(m):
     assert torch.equal(out, TC.dense_gemm_bf16(q, qs, wt.weight_mxfp4, wt.weight_shift2, wt.weight_channel_scale))
     assert torch.equal(D.mxfp4_int8_dense_forward(x, wt), out)
     assert D.check_device_status() == 0
+
+
+@pytest.mark.parametrize("kind", ["zipf", "uniform"])
+def test_prefill_gemms_repeat_bit_identical(weights, kind):
+    """Repeated full-size launches of the prefill GEMMs give identical bits.
+    A pipeline race shows up as an occasional corrupt tile (one launch in a
+    few), not as a stable error, so one launch per test is not enough: W13 +
+    SwiGLU and W2 run 6 times each and every run must equal the checker
+    (W2) or the first run (W13, whose checker comparison allows 1 ulp)."""
+    _, w = weights
+    m = 8192
+    ids, _ = _routing(m, 1200 if kind == "zipf" else 1300, kind)
+    x = G.randn_bf16((m, H), 77).to(DEV)
+    nv = m * TOPK
+    bm = D.select_sorted_block_m(m, TOPK, E)
+    kw = dict(hidden_size=H, intermediate_size=I, topk=TOPK, block_m=bm, num_valid_tokens=nv)
+    s, e, n = D.moe_align_block_size(ids.to(DEV), bm, E)
+    cap = s.numel()
+    q, qs = D.quantize_per_token_int8(x)
+    a13, s13, r13 = J.moe_sort_rows(q, qs, s, n, topk=TOPK, num_valid_tokens=nv)
+    sl = s.long()
+    valid = (torch.arange(cap, device=DEV) < int(n.item())) & (sl >= 0) & (sl < nv)
+    first = None
+    for _ in range(6):
+        inter = torch.zeros((cap, I), dtype=torch.bfloat16, device=DEV)
+        J.mxfp4_int8_moe_gemm_swiglu_sorted(a13, s13, r13, w.w13_mxfp4, w.w13_shift2,
+                                            w.w13_channel_scale, inter, s, e, n, **kw)
+        if first is None:
+            first = inter
+        else:
+            assert torch.equal(inter[valid], first[valid])
+    a2, s2, r2 = J.quantize_sorted_int8(first, s, n, num_valid_tokens=nv)
+    rows2 = a2.view(I // 128, cap, 128).permute(1, 0, 2).reshape(cap, I)
+    ref_pos, _ = TC.moe_gemm_bf16(rows2, s2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale, s, e, n,
+                                  block_m=bm, topk=TOPK, num_valid=nv, source_rows_are_slots=True,
+                                  by_position=True)
+    for _ in range(6):
+        routed = torch.empty((nv, H), dtype=torch.bfloat16, device=DEV)
+        J.mxfp4_int8_moe_gemm_sorted(a2, s2, r2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale,
+                                     routed, s, e, n, **kw)
+        assert torch.equal(routed[sl[valid]], ref_pos[valid])
+    assert D.check_device_status() == 0
