@@ -320,6 +320,41 @@ def run_workload(weights, m, kind, steps, warmup, dev, rank, world, hbm, tops_i8
     return res
 
 
+def run_from_logits(weights, m, steps, warmup, dev):
+    """The decode layer from router logits: the fused router top-k + expert
+    align launch (mxfp4_int8_moe_forward_from_logits) instead of the align
+    over precomputed ids; logits N(0,1), per-expert bias N(0,0.1)."""
+    import torch
+    import dsv4_b200 as D
+    gen = torch.Generator()
+    gen.manual_seed(1000)
+    logits = torch.randn(m, E, generator=gen).to(dev)
+    mgen = torch.Generator()
+    mgen.manual_seed(MODEL_SEED)
+    bias = (torch.randn(E, generator=mgen) * 0.1).to(dev)
+    import gen_inputs as G
+    x = G.randn_bf16((m, H), 2000).to(dev)
+
+    def step():
+        return D.mxfp4_int8_moe_forward_from_logits(x, weights, logits, TOPK, hidden_size=H,
+                                                    intermediate_size=I, router_bias=bias)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"workload": "decode layer from router logits (fused router top-k + align launch), "
+                        "M=64, sigmoid + bias routing",
+            "value": m / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "launches_per_step": LAUNCHES_PER_STEP}
+
+
 def run_ep(m, kind, steps, warmup, dev, rank, world, soak_steps=0):
     """Expert-parallel layer: this rank holds E/world experts and m tokens.
     Fixed-capacity exchange (capacity = m on every rank): no host
@@ -651,6 +686,7 @@ def main():
         for name, kind in (("prefill", "zipf"), ("prefill_uniform", "uniform")):
             legs[name] = run_workload(weights, PREFILL_M, kind, psteps, args.warmup, dev, rank,
                                       world, hbm, tops_i8, sample_clocks=True)
+    legs["from_logits"] = run_from_logits(weights, DECODE_M, args.steps, args.warmup, dev)
     del weights
     torch.cuda.empty_cache()
     dense = None if args.no_dense else run_dense(dev, max(3, args.steps // 10), args.warmup, hbm,
@@ -735,6 +771,7 @@ def main():
                     "h2d_bytes_per_step": pre["h2d"], "d2h_bytes_per_step": pre["d2h"],
                     "ms_per_step": pre["e2e_ms"]},
             "clocks": pre["clocks"]}
+    line["decode_from_logits"] = legs["from_logits"]
     if dense is not None:
         line["dense"] = dense
     if cpu is not None:

@@ -892,11 +892,19 @@ int dsv4_b200_ep_plan_fixed(const int32_t* topk_ids, const float* topk_weights,
                "bad topk / meta width / meta stride");
   DSV4_REQUIRE(send_src && send_meta && (m == 0 || (topk_ids && topk_weights && a_scale && pos)),
                "null pointer argument");
-  ep_plan_fixed_kernel<<<1, kEpPlanThreads, 0, as_stream(stream)>>>(
-      topk_ids, topk_weights, a_scale, static_cast<int>(m), static_cast<int>(topk),
-      static_cast<int>(num_experts), static_cast<int>(world), static_cast<int>(capacity),
-      send_src, send_meta, static_cast<int>(meta_words), meta_stride, pos);
-  return check_launch("ep_plan_fixed_kernel");
+  cudaStream_t st = as_stream(stream);
+  ep_plan_fixed_kernel<<<1, kEpPlanThreads, 0, st>>>(
+      topk_ids, static_cast<int>(m), static_cast<int>(topk), static_cast<int>(num_experts),
+      static_cast<int>(world), static_cast<int>(capacity), send_src, pos);
+  if (int r = check_launch("ep_plan_fixed_kernel")) return r;
+  const int64_t words = world * capacity * meta_words;
+  if (words == 0) return DSV4_OK;
+  const int64_t blocks = (words + 255) / 256 < 4096 ? (words + 255) / 256 : 4096;
+  ep_meta_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      topk_ids, topk_weights, a_scale, static_cast<int>(topk), static_cast<int>(num_experts),
+      static_cast<int>(world), static_cast<int>(capacity), send_src, send_meta,
+      static_cast<int>(meta_words), meta_stride);
+  return check_launch("ep_meta_kernel");
 }
 
 int dsv4_b200_ep_combine(const void* partial, const int64_t* pos, int64_t world, void* out,

@@ -628,29 +628,19 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* __restrict__ partial,
 // capacity, world <= 8).  For token t and rank r holding one of its experts,
 // the row goes to slot r*capacity + (number of earlier tokens that also go to
 // r).  Tokens are taken 1024 at a time; per-rank running counts carry over.
-// Outputs, per slot: the source token (-1 for padding) and a metadata row
-// {scale, topk local expert ids (-1 = not on r / padding), topk weights}
-// written at meta + slot * meta_stride (int32 words, so the rows can sit in
-// the tail of the packed send rows); per token: pos[t][r] = slot or -1.
+// Outputs: per slot the source token (-1 for padding), per token pos[t][r] =
+// slot or -1.  The metadata rows come from ep_meta_kernel (grid-wide).
 constexpr int kEpPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kEpPlanThreads, 1)
-ep_plan_fixed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w,
-                     const float* __restrict__ a_scale, int m, int topk, int num_experts,
+ep_plan_fixed_kernel(const int32_t* __restrict__ ids, int m, int topk, int num_experts,
                      int world, int capacity, int64_t* __restrict__ send_src,
-                     int32_t* __restrict__ meta, int meta_words, int64_t meta_stride,
                      int64_t* __restrict__ pos) {
   __shared__ int warp_cnt[8][32];
   __shared__ int run[8];
   const int t0 = threadIdx.x;
   const int lane = t0 & 31, wid = t0 >> 5;
   const int e_loc = num_experts / world;
-  // padding defaults for every slot
-  for (int sidx = t0; sidx < world * capacity; sidx += kEpPlanThreads) {
-    send_src[sidx] = -1;
-    int32_t* row = meta + static_cast<int64_t>(sidx) * meta_stride;
-    for (int c = 0; c < meta_words; ++c) row[c] = (c >= 1 && c <= topk) ? -1 : 0;
-  }
   if (t0 < 8) run[t0] = 0;
   __syncthreads();
   for (int base = 0; base < m; base += kEpPlanThreads) {
@@ -678,14 +668,6 @@ ep_plan_fixed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ 
           const int j = before + rank_in[r];
           slot = static_cast<int64_t>(r) * capacity + j;
           send_src[slot] = t;
-          int32_t* row = meta + slot * meta_stride;
-          row[0] = __float_as_int(a_scale[t]);
-          for (int k = 0; k < topk; ++k) {
-            const int e = ids[static_cast<int64_t>(t) * topk + k];
-            const bool mine = e >= 0 && e < num_experts && e / e_loc == r;
-            row[1 + k] = mine ? e - r * e_loc : -1;
-            row[1 + topk + k] = __float_as_int(mine ? w[static_cast<int64_t>(t) * topk + k] : 0.f);
-          }
         }
         pos[static_cast<int64_t>(t) * world + r] = slot;
       }
@@ -697,6 +679,43 @@ ep_plan_fixed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ 
       run[t0] += tot;
     }
     __syncthreads();
+  }
+  // padding slots
+  for (int r = 0; r < world; ++r)
+    for (int j = run[r] + t0; j < capacity; j += kEpPlanThreads)
+      send_src[static_cast<int64_t>(r) * capacity + j] = -1;
+}
+
+// Metadata rows of the fixed-capacity exchange, one thread per word, from the
+// slot plan: slot s (rank r = s / capacity) of token t = send_src[s] gets
+// {scale bits, local ids on r (-1 elsewhere), matching weights (0
+// elsewhere)}; padding slots (t < 0) get {0, -1 x topk, 0 x topk}.  Rows sit
+// meta_stride words apart.
+__global__ void ep_meta_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                               const float* __restrict__ a_scale, int topk, int num_experts,
+                               int world, int capacity, const int64_t* __restrict__ send_src,
+                               int32_t* __restrict__ meta, int meta_words, int64_t meta_stride) {
+  const int64_t total = static_cast<int64_t>(world) * capacity * meta_words;
+  const int e_loc = num_experts / world;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t slot = i / meta_words;
+    const int c = static_cast<int>(i - slot * meta_words);
+    const int r = static_cast<int>(slot / capacity);
+    const int64_t t = __ldg(send_src + slot);
+    int32_t v = (c >= 1 && c <= topk) ? -1 : 0;
+    if (t >= 0) {
+      if (c == 0) {
+        v = __float_as_int(__ldg(a_scale + t));
+      } else if (c <= 2 * topk) {
+        const int k = c <= topk ? c - 1 : c - 1 - topk;
+        const int e = __ldg(ids + t * topk + k);
+        const bool mine = e >= 0 && e < num_experts && e / e_loc == r;
+        if (c <= topk) v = mine ? e - r * e_loc : -1;
+        else v = __float_as_int(mine ? __ldg(w + t * topk + k) : 0.f);
+      }
+    }
+    meta[slot * meta_stride + c] = v;
   }
 }
 
