@@ -65,6 +65,17 @@ __device__ long long g_trace[kTraceEvents][kTraceStages];
   } while (0)
 #endif
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start before its predecessor in the stream finishes.
+// pdl_entry() lets the next kernel in the stream be scheduled early and then
+// waits until every predecessor has completed and its memory is visible, so
+// it must run before the kernel's first global-memory access.  Without that
+// launch attribute both instructions do nothing.
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -4,6 +4,8 @@
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
+#include <cstdlib>
+#include <utility>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -38,6 +40,35 @@ int check_launch(const char* what) {
   } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Kernels of the hot path are launched with programmatic stream
+// serialisation (each calls pdl_entry() before touching global memory), so a
+// kernel's launch and scheduling overlap its predecessor's tail.
+// DSV4_B200_PDL=0 turns the attribute off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("DSV4_B200_PDL");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  // errors surface through cudaGetLastError in check_launch
+  (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 constexpr int kMaxDevices = 64;
 std::mutex g_init_mu;
@@ -115,7 +146,7 @@ int launch_gemm(int tn, int64_t max_items, const TcGemmParams& p, cudaStream_t s
   switch (tn) {
 #define DSV4_CASE(T)                                                                    \
   case T:                                                                               \
-    mxfp4_int8_tc_gemm_kernel<T, EPI><<<grid, TcGemmCfg<T>::kThreads, GemmKernel<T, EPI>::kSmem, st>>>(p); \
+    launch_pdl(&mxfp4_int8_tc_gemm_kernel<T, EPI>, grid, TcGemmCfg<T>::kThreads, GemmKernel<T, EPI>::kSmem, st, p); \
     break;
     DSV4_CASE(16)
     DSV4_CASE(32)
@@ -516,26 +547,26 @@ int dsv4_b200_quantize_per_token_int8(const void* a, int dtype, int64_t m, int64
     const int rows_per_cta = wide ? 2 : 8;
     const dim3 g(static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta));
     if (dtype == DSV4_BF16) {
-      if (wide) quant_rows_reg_kernel<__nv_bfloat16, 128, 8><<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale);
-      else quant_rows_reg_kernel<__nv_bfloat16, 32, 8><<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale);
+      if (wide) launch_pdl(&quant_rows_reg_kernel<__nv_bfloat16, 128, 8>, g, 256, 0, st, static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
+      else launch_pdl(&quant_rows_reg_kernel<__nv_bfloat16, 32, 8>, g, 256, 0, st, static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
     } else {
-      if (wide) quant_rows_reg_kernel<__half, 128, 8><<<g, 256, 0, st>>>(static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale);
-      else quant_rows_reg_kernel<__half, 32, 8><<<g, 256, 0, st>>>(static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale);
+      if (wide) launch_pdl(&quant_rows_reg_kernel<__half, 128, 8>, g, 256, 0, st, static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
+      else launch_pdl(&quant_rows_reg_kernel<__half, 32, 8>, g, 256, 0, st, static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
     }
     return check_launch("quant_rows_reg_kernel");
   }
   const dim3 grid(static_cast<unsigned>((m + 7) / 8));
   switch (dtype) {
     case DSV4_F32:
-      quant_rows_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(a), m, k, lda,
+      launch_pdl(&quant_rows_kernel<float>, grid, 256, 0, st, static_cast<const float*>(a), m, k, lda,
                                                      clamp_abs, a_q, a_scale);
       break;
     case DSV4_F16:
-      quant_rows_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(a), m, k, lda,
+      launch_pdl(&quant_rows_kernel<__half>, grid, 256, 0, st, static_cast<const __half*>(a), m, k, lda,
                                                       clamp_abs, a_q, a_scale);
       break;
     case DSV4_BF16:
-      quant_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+      launch_pdl(&quant_rows_kernel<__nv_bfloat16>, grid, 256, 0, st, 
           static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale);
       break;
     default:
@@ -683,7 +714,7 @@ int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int64
                (long long)sorted_capacity, (long long)need);
   DSV4_REQUIRE(expert_ids_capacity * block_size >= need, "expert_ids capacity too small");
   const int smem = align_smem_bytes(static_cast<int>(num_experts));
-  moe_align_kernel<<<1, kAlignThreads, smem, as_stream(stream)>>>(
+  launch_pdl(&moe_align_kernel, 1, kAlignThreads, smem, as_stream(stream), 
       topk_ids, static_cast<int>(numel), static_cast<int>(num_experts),
       static_cast<int>(block_size), sorted_token_ids, static_cast<int>(sorted_capacity),
       expert_ids, static_cast<int>(expert_ids_capacity), num_tokens_post_pad, cumsum_buffer);
@@ -744,7 +775,7 @@ int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, int64_t m_i
                    (reinterpret_cast<uintptr_t>(out_q) & 15) == 0,
                "a_q and out_q must be 16-byte aligned");
   const int64_t blocks = (sorted_capacity + 7) / 8 < 4096 ? (sorted_capacity + 7) / 8 : 4096;
-  sort_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+  launch_pdl(&sort_rows_kernel, static_cast<unsigned>(blocks), 256, 0, as_stream(stream), 
       a_q, a_scale, m_in, k, lda, scale_stride, sorted_token_ids, num_tokens_post_padded,
       sorted_capacity,
       static_cast<int>(topk), source_rows_are_slots ? 1 : 0, static_cast<int>(num_valid_tokens),
@@ -773,7 +804,7 @@ int dsv4_b200_quantize_sorted_int8(const void* a, int dtype, int64_t k,
   const dim3 g(static_cast<unsigned>((sorted_capacity + rows_per_cta - 1) / rows_per_cta));
   const int nv = static_cast<int>(num_valid_tokens);
 #define DSV4_QS(T, RT)                                                                        \
-  quant_rows_reg_kernel<T, RT, 8><<<g, 256, 0, st>>>(static_cast<const T*>(a), sorted_capacity, \
+  launch_pdl(&quant_rows_reg_kernel<T, RT, 8>, g, 256, 0, st, static_cast<const T*>(a), sorted_capacity, \
                                                      k, k, 0.f, out_q, out_scale,               \
                                                      sorted_token_ids, num_tokens_post_padded,  \
                                                      nv, sorted_capacity, out_rowsum)
@@ -830,7 +861,7 @@ int dsv4_b200_mxfp4_int8_moe_reduce(const void* routed_out, const float* topk_we
   if (m_out == 0) return DSV4_OK;
   DSV4_REQUIRE(routed_out && topk_weights && out, "null pointer argument");
   const int64_t threads = m_out * (n / 8);
-  moe_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+  launch_pdl(&moe_reduce_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream), 
       static_cast<const __nv_bfloat16*>(routed_out), topk_weights,
       static_cast<__nv_bfloat16*>(out), static_cast<int>(m_out), static_cast<int>(n),
       static_cast<int>(topk), static_cast<int>(num_valid_tokens), routed_scaling_factor,
@@ -851,8 +882,8 @@ int dsv4_b200_mxfp4_int8_moe_reduce_masked(const void* routed_out, const float* 
   if (m_out == 0) return DSV4_OK;
   DSV4_REQUIRE(routed_out && topk_weights && topk_ids && out, "null pointer argument");
   const int64_t threads = m_out * (n / 8);
-  moe_reduce_masked_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
-                             as_stream(stream)>>>(
+  launch_pdl(&moe_reduce_masked_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0,
+                             as_stream(stream), 
       static_cast<const __nv_bfloat16*>(routed_out), topk_weights, topk_ids,
       static_cast<__nv_bfloat16*>(out), static_cast<int>(m_out), static_cast<int>(n),
       static_cast<int>(topk), static_cast<int>(num_valid_tokens), routed_scaling_factor,
@@ -954,8 +985,8 @@ int dsv4_b200_mxfp4_int8_dense_gemm(const int8_t* a_q, const float* a_scale, int
                              stream))
       return r;
     const int64_t total = m * n;
-    splitk_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0,
-                           as_stream(stream)>>>(partial, static_cast<int>(splits), split_stride,
+    launch_pdl(&splitk_reduce_kernel, static_cast<unsigned>((total + 255) / 256), 256, 0,
+                           as_stream(stream), partial, static_cast<int>(splits), split_stride,
                                                 partial_ld, a_scale, b_channel_scale,
                                                 static_cast<__nv_bfloat16*>(out),
                                                 static_cast<int>(m), static_cast<int>(n));
@@ -994,7 +1025,7 @@ int dsv4_b200_quantize_per_token_int8_cm(const void* a, int dtype, int64_t m, in
   const int rows_per_cta = wide ? 2 : 8;
   const dim3 g(static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta));
 #define DSV4_QC(T, RT)                                                                         \
-  quant_rows_reg_kernel<T, RT, 8><<<g, 256, 0, st>>>(static_cast<const T*>(a), m, k, k, 0.f, a_cm, \
+  launch_pdl(&quant_rows_reg_kernel<T, RT, 8>, g, 256, 0, st, static_cast<const T*>(a), m, k, k, 0.f, a_cm, \
                                                      a_scale, nullptr, nullptr, 0, m, a_rowsum)
   if (dtype == DSV4_BF16) {
     if (wide) DSV4_QC(__nv_bfloat16, 128); else DSV4_QC(__nv_bfloat16, 32);
@@ -1017,7 +1048,7 @@ int dsv4_b200_rows_to_cm(const int8_t* a_q, int64_t m, int64_t k, int64_t lda, i
                "a_q and a_cm must be 16-byte aligned");
   const int64_t blocks = (m + 7) / 8 < 4096 ? (m + 7) / 8 : 4096;
   // identity permutation: a_scale is not copied (the caller's stays valid)
-  sort_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+  launch_pdl(&sort_rows_kernel, static_cast<unsigned>(blocks), 256, 0, as_stream(stream), 
       a_q, nullptr, m, k, lda, 1, nullptr, nullptr, m, 1, 1, static_cast<int>(m), a_cm, nullptr,
       a_rowsum);
   return check_launch("sort_rows_kernel (identity)");

@@ -254,6 +254,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  pdl_entry();  // before the first global read (num_tokens_post_padded)
 
   // ---- the item space (identical in every thread) ----
   int n_blocks, n_items;

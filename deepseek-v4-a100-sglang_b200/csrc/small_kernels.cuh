@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ a
                                                          int64_t k, int64_t lda, float clamp_abs,
                                                          int8_t* __restrict__ q,
                                                          float* __restrict__ scale) {
+  pdl_entry();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= m) return;
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
                                                              const int32_t* __restrict__ ntpp = nullptr,
                                                              int num_valid = 0, int64_t cm_rows = 0,
                                                              int32_t* __restrict__ rowsum = nullptr) {
+  pdl_entry();
   constexpr int kRowsPerCta = 256 / RT;
   __shared__ float red[256 / 32];
   __shared__ int red_i[256 / 32];
@@ -199,6 +201,7 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
                                                         int num_valid, int8_t* __restrict__ out,
                                                         float* __restrict__ out_scale,
                                                         int32_t* __restrict__ out_rowsum) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const int64_t n = ntpp != nullptr ? min(cap, static_cast<int64_t>(__ldg(ntpp))) : cap;
   const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -321,6 +324,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
 moe_align_kernel(const int32_t* __restrict__ ids, int numel, int num_experts, int block_m,
                  int32_t* __restrict__ sorted_ids, int sorted_cap, int32_t* __restrict__ expert_ids,
                  int expert_cap, int32_t* __restrict__ ntpp, int32_t* __restrict__ cumsum_out) {
+  pdl_entry();
   extern __shared__ int sm_align[];
   const int E = num_experts;
   int* wc = sm_align;             // [32][E] per-warp counts, then placement cursors
@@ -511,6 +515,7 @@ __global__ void moe_reduce_kernel(const __nv_bfloat16* __restrict__ routed,
                                   const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                   int m_out, int n, int topk, int num_valid, float rsf,
                                   int apply_rsf) {
+  pdl_entry();
   const int chunks = n / 8;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<int64_t>(m_out) * chunks) return;
@@ -546,6 +551,7 @@ __global__ void moe_reduce_masked_kernel(const __nv_bfloat16* __restrict__ route
                                          const int32_t* __restrict__ ids,
                                          __nv_bfloat16* __restrict__ out, int m_out, int n,
                                          int topk, int num_valid, float rsf, int apply_rsf) {
+  pdl_entry();
   const int chunks = n / 8;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<int64_t>(m_out) * chunks) return;
@@ -860,6 +866,7 @@ __global__ void splitk_reduce_kernel(const int32_t* __restrict__ partial, int sp
                                      const float* __restrict__ a_scale,
                                      const float* __restrict__ cs, __nv_bfloat16* __restrict__ out,
                                      int m, int n) {
+  pdl_entry();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<int64_t>(m) * n) return;
   const int row = static_cast<int>(idx / n);
