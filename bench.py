@@ -169,8 +169,11 @@ class Layer:
         kw = dict(hidden_size=H, intermediate_size=I, topk=TOPK, block_m=self.bm,
                   num_valid_tokens=m * TOPK)
         s, e, n = D.moe_align_block_size(ids, self.bm, E)
-        q, qs = D.quantize_per_token_int8(x)
-        a13, s13, r13 = J.moe_sort_rows(q, qs, s, n, topk=TOPK, num_valid_tokens=m * TOPK)
+        if m <= 512:  # as mxfp4_int8_moe_forward: one quantise + sort launch at decode
+            a13, s13, r13 = J.quantize_sort_int8(x, s, n, topk=TOPK, num_valid_tokens=m * TOPK)
+        else:
+            q, qs = D.quantize_per_token_int8(x)
+            a13, s13, r13 = J.moe_sort_rows(q, qs, s, n, topk=TOPK, num_valid_tokens=m * TOPK)
         inter = torch.empty((s.numel(), I), device=self.dev, dtype=torch.bfloat16)
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
         if record:
@@ -197,7 +200,7 @@ class Layer:
         return statistics.mean(w13), statistics.mean(w2)
 
 
-LAUNCHES_PER_STEP = 7  # align, quant, sort rows, W13+SwiGLU, quant, W2, combine
+LAUNCHES_PER_STEP = 6  # decode: align, quant+sort, W13+SwiGLU, quant, W2, combine
 
 
 MODEL_SEED = 7  # router bias and expert popularity: properties of the model, shared by all ranks
@@ -827,7 +830,7 @@ def main_ep(args, dev, rank, world, hbm):
             "e2e": {"value": total / (dec["e2e_ms"] * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"],
                     "ms_per_step": dec["e2e_ms"]},
-            "gpu_launches": (LAUNCHES_PER_STEP + 3) * args.steps,
+            "gpu_launches": 11 * args.steps,  # quant, plan, meta, gather, align, sort, W13, quant, W2, reduce, combine
             "clocks": dec["clocks"],
         }
         for kind, r in pre.items():

@@ -454,7 +454,18 @@ cudaError_t set_router_align_attrs() {
         e = cudaFuncSetAttribute(router_align_fn(dt, epl),
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  route_align_smem_bytes(kAlignMaxExperts));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&moe_align_coop_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             route_align_smem_bytes(kAlignMaxExperts));
   return e;
+}
+
+// CTAs of the multi-CTA align: about 1,024 ids each, at most one per SM.
+int64_t align_coop_grid(int64_t numel) {
+  int64_t g = (numel + 1023) / 1024;
+  if (g < 1) g = 1;
+  return g < sm_count() ? g : sm_count();
 }
 
 // CTAs of the fused router + align: one per 64 tokens, at most one per SM
@@ -547,11 +558,11 @@ int dsv4_b200_quantize_per_token_int8(const void* a, int dtype, int64_t m, int64
     const int rows_per_cta = wide ? 2 : 8;
     const dim3 g(static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta));
     if (dtype == DSV4_BF16) {
-      if (wide) launch_pdl(&quant_rows_reg_kernel<__nv_bfloat16, 128, 8>, g, 256, 0, st, static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
-      else launch_pdl(&quant_rows_reg_kernel<__nv_bfloat16, 32, 8>, g, 256, 0, st, static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
+      if (wide) launch_pdl(&quant_rows_reg_kernel<__nv_bfloat16, 128, 8>, g, 256, 0, st, static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr, 0);
+      else launch_pdl(&quant_rows_reg_kernel<__nv_bfloat16, 32, 8>, g, 256, 0, st, static_cast<const __nv_bfloat16*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr, 0);
     } else {
-      if (wide) launch_pdl(&quant_rows_reg_kernel<__half, 128, 8>, g, 256, 0, st, static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
-      else launch_pdl(&quant_rows_reg_kernel<__half, 32, 8>, g, 256, 0, st, static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr);
+      if (wide) launch_pdl(&quant_rows_reg_kernel<__half, 128, 8>, g, 256, 0, st, static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr, 0);
+      else launch_pdl(&quant_rows_reg_kernel<__half, 32, 8>, g, 256, 0, st, static_cast<const __half*>(a), m, k, lda, clamp_abs, a_q, a_scale, nullptr, nullptr, 0, 0, nullptr, 0);
     }
     return check_launch("quant_rows_reg_kernel");
   }
@@ -721,6 +732,52 @@ int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int64
   return check_launch("moe_align_kernel");
 }
 
+int dsv4_b200_moe_align_workspace_words(int64_t numel, int64_t num_experts, int64_t* words) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(words != nullptr && numel >= 0 && num_experts >= 1, "bad arguments");
+  *words = align_coop_grid(numel) * num_experts;
+  return DSV4_OK;
+}
+
+int dsv4_b200_moe_align_block_size_ws(const int32_t* topk_ids, int64_t numel,
+                                      int64_t num_experts, int64_t block_size,
+                                      int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                      int32_t* expert_ids, int64_t expert_ids_capacity,
+                                      int32_t* num_tokens_post_pad, int32_t* cumsum_buffer,
+                                      int32_t* workspace, int64_t workspace_words,
+                                      void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(num_experts >= 1 && num_experts <= kAlignMaxExperts,
+               "num_experts must be in [1, %d], got %lld", kAlignMaxExperts,
+               (long long)num_experts);
+  DSV4_REQUIRE(block_size >= 1 && block_size <= 1024, "bad block_size %lld",
+               (long long)block_size);
+  DSV4_REQUIRE(numel >= 0 && numel < (1ll << 30), "bad numel %lld", (long long)numel);
+  DSV4_REQUIRE(num_tokens_post_pad && (topk_ids || numel == 0) &&
+                   (sorted_token_ids || sorted_capacity == 0) &&
+                   (expert_ids || expert_ids_capacity == 0),
+               "null pointer argument");
+  const int64_t need = align_capacity(numel, num_experts, block_size);
+  DSV4_REQUIRE(sorted_capacity >= need, "sorted_token_ids capacity %lld < %lld",
+               (long long)sorted_capacity, (long long)need);
+  DSV4_REQUIRE(expert_ids_capacity * block_size >= need, "expert_ids capacity too small");
+  const int64_t grid = align_coop_grid(numel);
+  DSV4_REQUIRE(workspace != nullptr && workspace_words >= grid * num_experts,
+               "workspace needs %lld int32 words", (long long)(grid * num_experts));
+  int numel_i = static_cast<int>(numel), e_i = static_cast<int>(num_experts);
+  int bm_i = static_cast<int>(block_size), ipc = static_cast<int>((numel + grid - 1) / grid);
+  int cap_i = static_cast<int>(sorted_capacity), ecap_i = static_cast<int>(expert_ids_capacity);
+  void* args[] = {&topk_ids, &numel_i, &e_i, &bm_i, &ipc, &sorted_token_ids, &cap_i,
+                  &expert_ids, &ecap_i, &num_tokens_post_pad, &cumsum_buffer, &workspace};
+  cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&moe_align_coop_kernel),
+                                              dim3(static_cast<unsigned>(grid)),
+                                              dim3(kRouteAlignThreads), args,
+                                              route_align_smem_bytes(e_i), as_stream(stream));
+  if (e != cudaSuccess)
+    return fail(DSV4_ERR_CUDA, "moe_align_coop_kernel: %s", cudaGetErrorString(e));
+  return DSV4_OK;
+}
+
 int dsv4_b200_mxfp4_int8_moe_gemm(const int8_t* a_q, const float* a_scale, int64_t m_in,
                                   const uint8_t* b_mxfp4, const uint8_t* b_shift2,
                                   const float* b_channel_scale, int64_t num_experts, int64_t n,
@@ -807,7 +864,7 @@ int dsv4_b200_quantize_sorted_int8(const void* a, int dtype, int64_t k,
   launch_pdl(&quant_rows_reg_kernel<T, RT, 8>, g, 256, 0, st, static_cast<const T*>(a), sorted_capacity, \
                                                      k, k, 0.f, out_q, out_scale,               \
                                                      sorted_token_ids, num_tokens_post_padded,  \
-                                                     nv, sorted_capacity, out_rowsum)
+                                                     nv, sorted_capacity, out_rowsum, 0)
   if (dtype == DSV4_BF16) {
     if (wide) DSV4_QS(__nv_bfloat16, 128); else DSV4_QS(__nv_bfloat16, 32);
   } else {
@@ -815,6 +872,43 @@ int dsv4_b200_quantize_sorted_int8(const void* a, int dtype, int64_t k,
   }
 #undef DSV4_QS
   return check_launch("quant_rows_reg_kernel (sorted)");
+}
+
+int dsv4_b200_quantize_sort_int8(const void* a, int dtype, int64_t m_in, int64_t k,
+                                 const int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                 const int32_t* num_tokens_post_padded, int64_t topk,
+                                 int64_t num_valid_tokens, int8_t* out_q, float* out_scale,
+                                 int32_t* out_rowsum, void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(dtype == DSV4_BF16 || dtype == DSV4_F16, "a must be bf16 or fp16 (dtype %d)", dtype);
+  DSV4_REQUIRE(k > 0 && k % 128 == 0 && k <= 8192, "K must be a multiple of 128 in [128, 8192]");
+  DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
+  DSV4_REQUIRE(m_in >= 0 && num_valid_tokens >= 0 && num_valid_tokens <= m_in * topk &&
+                   num_valid_tokens < (1ll << 31),
+               "token rows do not cover num_valid_tokens");
+  if (sorted_capacity == 0 || m_in == 0) return DSV4_OK;
+  DSV4_REQUIRE(a && sorted_token_ids && num_tokens_post_padded && out_q && out_scale && out_rowsum,
+               "null pointer argument");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out_q) & 7) == 0,
+               "a must be 16-byte and out_q 8-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const bool wide = k > 2048;
+  const int rows_per_cta = wide ? 2 : 8;
+  const dim3 g(static_cast<unsigned>((sorted_capacity + rows_per_cta - 1) / rows_per_cta));
+  const int nv = static_cast<int>(num_valid_tokens);
+  const int tk = static_cast<int>(topk);
+#define DSV4_QG(T, RT)                                                                          \
+  launch_pdl(&quant_rows_reg_kernel<T, RT, 8>, g, 256, 0, st, static_cast<const T*>(a),          \
+             sorted_capacity, k, k, 0.f, out_q, out_scale, sorted_token_ids,                     \
+             num_tokens_post_padded, nv, sorted_capacity, out_rowsum, tk)
+  if (dtype == DSV4_BF16) {
+    if (wide) DSV4_QG(__nv_bfloat16, 128); else DSV4_QG(__nv_bfloat16, 32);
+  } else {
+    if (wide) DSV4_QG(__half, 128); else DSV4_QG(__half, 32);
+  }
+#undef DSV4_QG
+  return check_launch("quant_rows_reg_kernel (quantise + sort)");
 }
 
 int dsv4_b200_mxfp4_int8_moe_gemm_sorted(
@@ -1026,7 +1120,7 @@ int dsv4_b200_quantize_per_token_int8_cm(const void* a, int dtype, int64_t m, in
   const dim3 g(static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta));
 #define DSV4_QC(T, RT)                                                                         \
   launch_pdl(&quant_rows_reg_kernel<T, RT, 8>, g, 256, 0, st, static_cast<const T*>(a), m, k, k, 0.f, a_cm, \
-                                                     a_scale, nullptr, nullptr, 0, m, a_rowsum)
+                                                     a_scale, nullptr, nullptr, 0, m, a_rowsum, 0)
   if (dtype == DSV4_BF16) {
     if (wide) DSV4_QC(__nv_bfloat16, 128); else DSV4_QC(__nv_bfloat16, 32);
   } else {

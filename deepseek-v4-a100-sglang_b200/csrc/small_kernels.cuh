@@ -102,7 +102,8 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
                                                              const int32_t* __restrict__ sorted = nullptr,
                                                              const int32_t* __restrict__ ntpp = nullptr,
                                                              int num_valid = 0, int64_t cm_rows = 0,
-                                                             int32_t* __restrict__ rowsum = nullptr) {
+                                                             int32_t* __restrict__ rowsum = nullptr,
+                                                             int gather_topk = 0) {
   pdl_entry();
   constexpr int kRowsPerCta = 256 / RT;
   __shared__ float red[256 / 32];
@@ -111,15 +112,19 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
   const int lt = threadIdx.x % RT;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerCta + r_local;
   bool active = row < m;
+  // source row: the row itself, or (gather_topk > 0, the fused quantise +
+  // sort of the token rows) the token of the routed slot at this position
+  int64_t src_row = row;
   if (sorted != nullptr && active) {
     const int slot = row < __ldg(ntpp) ? __ldg(sorted + row) : -1;
     active = slot >= 0 && slot < num_valid;
+    if (gather_topk > 0) src_row = active ? slot / gather_topk : 0;
   }
   const int nv = static_cast<int>(k / 8);
   uint4 u[VPT];
   float amax = 0.f;
   if (active) {
-    const uint4* xv = reinterpret_cast<const uint4*>(a + row * lda);
+    const uint4* xv = reinterpret_cast<const uint4*>(a + src_row * lda);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int idx = lt + i * RT;
@@ -855,6 +860,129 @@ router_align_kernel(const T* __restrict__ logits, int m, int num_experts,
       if (pos < sorted_cap) sorted_ids[pos] = t * topk + lane;
       wc[warp * E + e] += 1;
     }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// a5, multi-CTA form (cooperative launch) for large inputs: the same outputs
+// as moe_align_kernel, bit for bit.  CTA c owns flat ids [c*ipc, (c+1)*ipc),
+// its warps contiguous sub-ranges, so (CTA, warp, index) is the slot order.
+//   phase 1  per-(warp, expert) counts in shared memory (ids outside [0, E)
+//            dropped), per-(CTA, expert) totals to `cta_counts`; padding fill
+//   grid sync
+//   phase 2  CTA base per expert, padded prefix over experts; expert_ids,
+//            num_tokens_post_pad, cumsum
+//   phase 3  placement, 32 ids at a time: __match_any groups equal experts,
+//            the rank among lower lanes gives the position
+// Shared memory: route_align_smem_bytes(E).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kRouteAlignThreads, 1)
+moe_align_coop_kernel(const int32_t* __restrict__ ids, int numel, int num_experts, int block_m,
+                      int ipc, int32_t* __restrict__ sorted_ids, int sorted_cap,
+                      int32_t* __restrict__ expert_ids, int expert_cap,
+                      int32_t* __restrict__ ntpp, int32_t* __restrict__ cumsum_out,
+                      int32_t* __restrict__ cta_counts) {
+  extern __shared__ int sm_ac[];
+  const int E = num_experts;
+  int* wc = sm_ac;
+  int* cbase = wc + 32 * E;
+  int* ebase = cbase + E;
+  int* scan = ebase + E + 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x, G = gridDim.x;
+  const int i_begin = min(numel, c * ipc), i_end = min(numel, i_begin + ipc);
+  const int ipw = (ipc + 31) / 32;
+  const int w_begin = min(i_end, i_begin + warp * ipw), w_end = min(i_end, w_begin + ipw);
+
+  for (int i = tid; i < 32 * E; i += kRouteAlignThreads) wc[i] = 0;
+  for (int i = c * kRouteAlignThreads + tid; i < sorted_cap; i += G * kRouteAlignThreads)
+    sorted_ids[i] = numel;
+  __syncthreads();
+  for (int i = w_begin + lane; i < w_end; i += 32) {
+    const int e = __ldg(ids + i);
+    if (e >= 0 && e < E) atomicAdd(&wc[warp * E + e], 1);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kRouteAlignThreads) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int v = wc[w * E + e];
+      wc[w * E + e] = run;
+      run += v;
+    }
+    cta_counts[static_cast<int64_t>(c) * E + e] = run;
+  }
+  cooperative_groups::this_grid().sync();
+  int cnt = 0;
+  if (tid < E) {
+    int before = 0, total = 0;
+    for (int q = 0; q < G; ++q) {
+      const int v = __ldcg(cta_counts + static_cast<int64_t>(q) * E + tid);
+      if (q < c) before += v;
+      total += v;
+    }
+    cbase[tid] = before;
+    cnt = total;
+  }
+  {
+    const int padded = (cnt + block_m - 1) / block_m * block_m;
+    int v = padded;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) scan[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int w = scan[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      scan[lane] = w;
+    }
+    __syncthreads();
+    const int incl = v + (warp > 0 ? scan[warp - 1] : 0);
+    if (tid < E) ebase[tid] = incl - padded;
+    if (tid == E - 1) ebase[E] = incl;
+  }
+  __syncthreads();
+  const int total = ebase[E];
+  for (int b = c * kRouteAlignThreads + tid; b < expert_cap; b += G * kRouteAlignThreads) {
+    int e = -1;
+    const int pos = b * block_m;
+    if (pos < total) {
+      int lo = 0, hi = E - 1;  // last e with ebase[e] <= pos
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (ebase[mid] <= pos) lo = mid; else hi = mid - 1;
+      }
+      e = lo;
+    }
+    expert_ids[b] = e;
+  }
+  if (c == 0) {
+    if (tid == 0) ntpp[0] = total;
+    if (cumsum_out != nullptr)
+      for (int e = tid; e <= E; e += kRouteAlignThreads) cumsum_out[e] = ebase[e];
+  }
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int i0 = w_begin; i0 < w_end; i0 += 32) {
+    const int i = i0 + lane;
+    const int e = i < w_end ? __ldg(ids + i) : -1;
+    const bool valid = e >= 0 && e < E;
+    const int key = valid ? e : (E + lane);  // unique key for invalid lanes
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int rank = __popc(peers & lt_mask);
+    if (valid) {
+      const int pos = ebase[e] + cbase[e] + wc[warp * E + e] + rank;
+      if (pos < sorted_cap) sorted_ids[pos] = i;
+    }
+    __syncwarp();
+    if (valid && rank == 0) wc[warp * E + e] += __popc(peers);
     __syncwarp();
   }
 }

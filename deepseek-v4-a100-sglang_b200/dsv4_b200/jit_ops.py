@@ -192,6 +192,28 @@ def moe_sort_rows(a_q, a_scale, sorted_token_ids, num_tokens_post_padded, *, top
     return q, sc, rs
 
 
+def quantize_sort_int8(a, sorted_token_ids, num_tokens_post_padded, *, topk: int,
+                       num_valid_tokens: int):
+    """Per-token INT8 quantisation of the bf16/fp16 token rows ``a`` [M, K]
+    fused with :func:`moe_sort_rows`: position p receives token
+    ``sorted_token_ids[p] // topk`` quantised, with its scale and row sum,
+    in the K-chunk-major layout.  One launch instead of two."""
+    _check(a.dim() == 2 and a.dtype in (torch.bfloat16, torch.float16) and a.is_contiguous(),
+           "a must be a contiguous 2-D bf16/fp16 tensor")
+    _check(a.is_cuda, "a must be a CUDA tensor (no CPU path)")
+    m, k = a.shape
+    cap = sorted_token_ids.numel()
+    q = torch.empty(cap * k, device=a.device, dtype=torch.int8)
+    sc = torch.empty(cap, device=a.device, dtype=torch.float32)
+    rs = torch.empty(cap, device=a.device, dtype=torch.int32)
+    _init_device(a.device)
+    N.call("dsv4_b200_quantize_sort_int8", a.data_ptr(),
+           N.DTYPE_BF16 if a.dtype == torch.bfloat16 else N.DTYPE_F16, m, k,
+           sorted_token_ids.data_ptr(), cap, num_tokens_post_padded.data_ptr(), topk,
+           num_valid_tokens, q.data_ptr(), sc.data_ptr(), rs.data_ptr(), N.stream_of(a))
+    return q, sc, rs
+
+
 def quantize_sorted_int8(a, sorted_token_ids, num_tokens_post_padded, *, num_valid_tokens: int):
     """Per-token INT8 quantisation of sorted-position rows ``a``
     ``[sorted_capacity, K]`` (bf16/fp16) into ``(q, scale, rowsum)`` as

@@ -23,6 +23,7 @@ from .jit_ops import (
     mxfp4_int8_dense_gemm,
     prewarm_mxfp4_int8_moe_jit_modules,
     moe_sort_rows,
+    quantize_sort_int8,
     quantize_sorted_int8,
     mxfp4_int8_moe_gemm_swiglu_sorted,
     mxfp4_int8_moe_gemm_sorted,
@@ -321,10 +322,27 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
     n_blocks = (cap + block_size - 1) // block_size
     expert_ids = torch.empty((n_blocks,), dtype=torch.int32, device=dev)
     ntpp = torch.empty((1,), dtype=torch.int32, device=dev)
+    if numel >= _ALIGN_COOP_MIN_IDS:
+        # many ids: the multi-CTA align (same outputs)
+        import ctypes
+        words = ctypes.c_int64(0)
+        N.call("dsv4_b200_moe_align_workspace_words", numel, num_experts, ctypes.byref(words))
+        ws = torch.empty((max(words.value, 1),), dtype=torch.int32, device=dev)
+        N.call("dsv4_b200_moe_align_block_size_ws", ids.data_ptr(), numel, num_experts,
+               block_size, sorted_ids.data_ptr(), cap, expert_ids.data_ptr(), n_blocks,
+               ntpp.data_ptr(), None, ws.data_ptr(), ws.numel(), N.stream_of(ids))
+        return sorted_ids, expert_ids, ntpp
     N.call("dsv4_b200_moe_align_block_size", ids.data_ptr() if numel else None, numel, num_experts,
            block_size, sorted_ids.data_ptr(), cap, expert_ids.data_ptr(), n_blocks,
            ntpp.data_ptr(), None, N.stream_of(ids))
     return sorted_ids, expert_ids, ntpp
+
+
+# tokens up to which the layer quantises and sorts in one launch
+_FUSED_QUANT_SORT_MAX_TOKENS = 512
+
+# ids from which moe_align_block_size runs the multi-CTA kernel
+_ALIGN_COOP_MIN_IDS = 8192
 
 
 _moe_align_block_size = moe_align_block_size
@@ -335,7 +353,8 @@ def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWei
                            intermediate_size: int, routed_scaling_factor: float | None = None,
                            clamp_limit: float | None = None,
                            apply_router_weight_on_input: bool = False) -> torch.Tensor:
-    """PYMOE:880-959.  Launches: align, quant, W13 GEMM with fused SwiGLU,
+    """PYMOE:880-959.  Launches: align, quant fused with the sort into expert
+    order, W13 GEMM with fused SwiGLU,
     quant, W2 GEMM, top-k combine with the routed scaling fused."""
     if apply_router_weight_on_input:
         raise NotImplementedError(
@@ -352,12 +371,11 @@ def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWei
     _, block_n = _select_moe_tile_shape(m, topk, experts)
     block_m = select_sorted_block_m(m, topk, experts)
     sorted_ids, expert_ids, ntpp = moe_align_block_size(topk_ids_i32, block_m, experts)
-    a13_q, a13_scale = quantize_per_token_int8(hidden_states, 0.0)
-    return _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids,
+    return _moe_core(None, None, weights, topk_ids_i32, topk_weights_f32, sorted_ids,
                      expert_ids, ntpp, block_m=block_m, block_n=block_n, hidden_size=hidden_size,
                      intermediate_size=intermediate_size,
                      routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
-                     masked=False)
+                     masked=False, hidden=hidden_states)
 
 
 def mxfp4_int8_moe_forward_from_logits(hidden_states: torch.Tensor,
@@ -381,30 +399,38 @@ def mxfp4_int8_moe_forward_from_logits(hidden_states: torch.Tensor,
     block_m = select_sorted_block_m(m, topk, experts)
     ids, w, sorted_ids, expert_ids, ntpp = router_align(router_logits, topk, block_m,
                                                         bias=router_bias, renormalize=renormalize)
-    a13_q, a13_scale = quantize_per_token_int8(hidden_states, 0.0)
-    out = _moe_core(a13_q, a13_scale, weights, ids, w, sorted_ids, expert_ids, ntpp,
+    out = _moe_core(None, None, weights, ids, w, sorted_ids, expert_ids, ntpp,
                     block_m=block_m, block_n=block_n, hidden_size=hidden_size,
                     intermediate_size=intermediate_size,
                     routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
-                    masked=False)
+                    masked=False, hidden=hidden_states)
     return out, ids, w
 
 
 def _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids, expert_ids,
               ntpp, *, block_m, block_n, hidden_size, intermediate_size, routed_scaling_factor,
-              clamp_limit, masked):
+              clamp_limit, masked, hidden=None):
     """W13 + SwiGLU, requantisation and W2 of mxfp4_int8_moe_forward
     (PYMOE:904-958) on expert-sorted rows: the routed token rows are copied
     once into the order of the aligned permutation (K-chunk-major), so each
     GEMM stage loads its token tile with one tensor-map copy.  Same results as
     the slot-addressed JIT entry points, bit for bit."""
-    m = a13_q.shape[0]
+    m = (hidden if hidden is not None else a13_q).shape[0]
     topk = topk_ids_i32.shape[1]
-    dev = a13_q.device
+    dev = topk_ids_i32.device
     nv = m * topk
     kw = dict(hidden_size=hidden_size, intermediate_size=intermediate_size, topk=topk,
               block_m=block_m, num_valid_tokens=nv)
-    a13, s13, r13 = moe_sort_rows(a13_q, a13_scale, sorted_ids, ntpp, topk=topk, num_valid_tokens=nv)
+    if hidden is not None and m <= _FUSED_QUANT_SORT_MAX_TOKENS:
+        # few tokens: quantise and sort in one launch (each routed copy of a
+        # token is quantised again; cheap at decode, not at prefill)
+        a13, s13, r13 = quantize_sort_int8(hidden, sorted_ids, ntpp, topk=topk,
+                                           num_valid_tokens=nv)
+    else:
+        if hidden is not None:
+            a13_q, a13_scale = quantize_per_token_int8(hidden, 0.0)
+        a13, s13, r13 = moe_sort_rows(a13_q, a13_scale, sorted_ids, ntpp, topk=topk,
+                                      num_valid_tokens=nv)
     inter = torch.empty((sorted_ids.numel(), intermediate_size), device=dev, dtype=torch.bfloat16)
     mxfp4_int8_moe_gemm_swiglu_sorted(a13, s13, r13, weights.w13_mxfp4, weights.w13_shift2,
                                       weights.w13_channel_scale, inter, sorted_ids, expert_ids,

@@ -126,6 +126,22 @@ DSV4_API int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t num
                                    int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
                                    int32_t* cumsum_buffer, void* stream);
 
+/* Multi-CTA form of dsv4_b200_moe_align_block_size (one cooperative launch,
+ * same outputs bit for bit) for large inputs: the library's op uses it from
+ * 8,192 ids up.  `workspace` holds per-CTA expert counts: at least the
+ * int32 words dsv4_b200_moe_align_workspace_words(numel, num_experts)
+ * reports; nothing in it needs to start at zero. */
+DSV4_API int dsv4_b200_moe_align_workspace_words(int64_t numel, int64_t num_experts,
+                                                 int64_t* words);
+DSV4_API int dsv4_b200_moe_align_block_size_ws(const int32_t* topk_ids, int64_t numel,
+                                               int64_t num_experts, int64_t block_size,
+                                               int32_t* sorted_token_ids,
+                                               int64_t sorted_capacity, int32_t* expert_ids,
+                                               int64_t expert_ids_capacity,
+                                               int32_t* num_tokens_post_pad,
+                                               int32_t* cumsum_buffer, int32_t* workspace,
+                                               int64_t workspace_words, void* stream);
+
 /* a6/a8. Grouped MXFP4 x INT8 GEMM over the aligned permutation:
  *   dst[slot][n] = bf16((f32(sum_k a_q[src][k] * W[e][n][k]) * a_scale[src]) * cs[e][n])
  * src = slot (source_rows_are_slots, W2) or slot / topk (W13).  dst has
@@ -190,6 +206,18 @@ DSV4_API int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, in
 /* Per-token INT8 quantisation (a1, PYMOE:46-66 arithmetic, no clamp) of the
  * sorted-position rows a [sorted_capacity][k] (bf16 or fp16), written
  * K-chunk-major.  The W2 input requantisation of PYMOE:937. */
+/* Per-token INT8 quantisation fused with the sort into expert order: the
+ * quantiser of dsv4_b200_quantize_per_token_int8 (PYMOE:53-126) applied to
+ * token row sorted_token_ids[p] / topk of `a` [m_in][k] (bf16/fp16) and
+ * written to position p of the K-chunk-major layout, with scale and row sum,
+ * i.e. what quantize_per_token_int8 followed by dsv4_b200_moe_sort_rows
+ * produce, in one launch.  Padding positions are left unwritten. */
+DSV4_API int dsv4_b200_quantize_sort_int8(const void* a, int dtype, int64_t m_in, int64_t k,
+                                          const int32_t* sorted_token_ids,
+                                          int64_t sorted_capacity,
+                                          const int32_t* num_tokens_post_padded, int64_t topk,
+                                          int64_t num_valid_tokens, int8_t* out_q,
+                                          float* out_scale, int32_t* out_rowsum, void* stream);
 DSV4_API int dsv4_b200_quantize_sorted_int8(const void* a, int dtype, int64_t k,
                                             const int32_t* sorted_token_ids,
                                             int64_t sorted_capacity,

@@ -100,6 +100,11 @@ def _run_layer_stages(weights, m, kind, seed):
     assert torch.equal(rows13[valid], q[slots // TOPK])
     assert torch.equal(s13[valid], qs[slots // TOPK])
     assert torch.equal(r13[valid].long(), q[slots // TOPK].long().sum(1))
+    # the fused quantise + sort gives the same rows, scales and sums
+    fa13, fs13, fr13 = J.quantize_sort_int8(xd, s, n, topk=TOPK, num_valid_tokens=nv)
+    frows = fa13.view(H // 128, cap, 128).permute(1, 0, 2).reshape(cap, H)
+    assert torch.equal(frows[valid], rows13[valid])
+    assert torch.equal(fs13[valid], s13[valid]) and torch.equal(fr13[valid], r13[valid])
 
     # W13 + SwiGLU (rows by sorted position)
     inter = torch.zeros((cap, I), dtype=torch.bfloat16, device=DEV)

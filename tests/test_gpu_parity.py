@@ -87,7 +87,9 @@ def test_repack_golden(golden, name, variant):
 
 @pytest.mark.parametrize("tokens,experts,topk,bm,drop", [
     (13, 4, 2, 16, False), (64, 256, 8, 16, False), (1, 8, 2, 16, False),
-    (8192, 256, 8, 128, False), (300, 32, 4, 64, True), (0, 8, 2, 16, False)])
+    (8192, 256, 8, 128, False), (300, 32, 4, 64, True), (0, 8, 2, 16, False),
+    # from 8,192 ids the multi-CTA align runs: with dropped ids, many experts
+    (5000, 64, 4, 64, True), (40000, 1024, 8, 256, False)])
 def test_align_bit_exact(tokens, experts, topk, bm, drop):
     rng = np.random.default_rng(tokens + experts)
     ids = rng.integers(0, experts, (tokens, topk)).astype(np.int32)
