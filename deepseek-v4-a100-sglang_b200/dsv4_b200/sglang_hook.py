@@ -25,6 +25,7 @@ from collections import namedtuple
 
 import torch
 
+from ._native import check_device_status
 from .mxfp4_int8_moe import mxfp4_int8_moe_forward, prepare_mxfp4_int8_moe
 
 BACKEND_TAG = "b200_mxfp4_int8"
@@ -108,6 +109,9 @@ def apply(method, layer: torch.nn.Module, dispatch_output):
         clamp_limit=getattr(cfg, "swiglu_limit", None),
         apply_router_weight_on_input=bool(getattr(cfg, "apply_router_weight_on_input", False)),
     )
+    if os.environ.get("DSV4_B200_CHECK_STATUS", "0") == "1":
+        # synchronises: raises DeviceTimeoutError if a kernel gave up a wait
+        check_device_status()
     return _combine_input(out)
 
 

@@ -330,10 +330,13 @@ def test_router_topk_matches_torch(m, e, topk, dtype):
         assert bool((s_ids[:, :-1] >= s_ids[:, 1:]).all())
 
 
-def test_sglang_hook_matches_forward(golden):
+def test_sglang_hook_matches_forward(golden, monkeypatch):
     """The SGLang hook (PATCH:450-581) prepares the layer and returns exactly
-    mxfp4_int8_moe_forward's output, with the config's scaling and clamp."""
+    mxfp4_int8_moe_forward's output, with the config's scaling and clamp; with
+    DSV4_B200_CHECK_STATUS=1 it also reads the device status word after the
+    layer (clean here, so nothing is raised)."""
     import types
+    monkeypatch.setenv("DSV4_B200_CHECK_STATUS", "1")
     import dsv4_b200.sglang_hook as H
     g = golden("moe_ref_small")
     layer = torch.nn.Module()
