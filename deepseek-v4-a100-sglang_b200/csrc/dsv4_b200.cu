@@ -92,6 +92,7 @@ cudaError_t set_attrs_epi() {
   one(GemmKernel<32, EPI>::fn(), GemmKernel<32, EPI>::kSmem);
   one(GemmKernel<64, EPI>::fn(), GemmKernel<64, EPI>::kSmem);
   one(GemmKernel<128, EPI>::fn(), GemmKernel<128, EPI>::kSmem);
+  one(GemmKernel<192, EPI>::fn(), GemmKernel<192, EPI>::kSmem);
   one(GemmKernel<256, EPI>::fn(), GemmKernel<256, EPI>::kSmem);
   return e;
 }
@@ -152,6 +153,7 @@ int launch_gemm(int tn, int64_t max_items, const TcGemmParams& p, cudaStream_t s
     DSV4_CASE(32)
     DSV4_CASE(64)
     DSV4_CASE(128)
+    DSV4_CASE(192)
     DSV4_CASE(256)
 #undef DSV4_CASE
     default:
@@ -250,7 +252,7 @@ int shift_chunk_rows(int stages_per_item, int tn) {
 //   b_mode 2: int8 K-chunk-major [k/128][rows][128] as 3-D {128, rows, k/128},
 //             box {128, tn, 2} (both 128-K halves of a stage in one copy)
 int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, int b_mode, int tn) {
-  DSV4_REQUIRE(tn <= 128 || b_mode == 2, "256-token tiles need K-chunk-major token rows");
+  DSV4_REQUIRE(tn <= 128 || b_mode == 2, "192/256-token tiles need K-chunk-major token rows");
   if (tensor_map_encoder() == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, "a_q must be 16-byte aligned");
   DSV4_REQUIRE(rows >= 1 && rows < (1ll << 31), "bad activation row count");
@@ -306,8 +308,8 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(dst) & 15) == 0, "output must be 16-byte aligned");
   DSV4_REQUIRE(topk >= 1 && topk <= 8, "topk must be in [1, 8], got %lld", (long long)topk);
   DSV4_REQUIRE(block_m == 16 || block_m == 32 || block_m == 64 || block_m == 128 ||
-                   (sorted_rows && block_m == 256),
-               "block_m must be 16, 32, 64, or 128 (or 256 for sorted rows), got %lld",
+                   (sorted_rows && (block_m == 192 || block_m == 256)),
+               "block_m must be 16, 32, 64, or 128 (or 192 / 256 for sorted rows), got %lld",
                (long long)block_m);
   DSV4_REQUIRE(num_valid >= 0, "num_valid_tokens must be non-negative");
   const int64_t max_m = align_capacity(num_valid, experts, block_m);

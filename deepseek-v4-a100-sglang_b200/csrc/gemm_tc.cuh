@@ -147,10 +147,12 @@ struct TcGemmCfg {
   // epilogue warps: 4, or 8 for 256-token tiles (two groups of 4 take
   // alternate 16-column chunks: that epilogue cannot overlap the next item's
   // MMAs, so its length counts in full)
-  static constexpr int kEpiWarps = TN >= 256 ? 8 : 4;
+  static constexpr int kEpiWarps = TN >= 192 ? 8 : 4;
   // A ring (decoded weights in TMEM, 64 columns = 256 K per slot) and B ring
   // (token tiles in shared memory) have their own depths and barriers
-  static constexpr int kStagesA = TN <= 64 ? 6 : 4;
+  // (192-token tiles: a 2-slot A ring leaves TMEM room for two accumulators,
+  // so the next item's MMAs overlap the epilogue; the decode runs far ahead)
+  static constexpr int kStagesA = TN <= 64 ? 6 : (TN == 192 ? 2 : 4);
   static constexpr int kStagesB = TN <= 64 ? 6 : (TN <= 128 ? 4 : 2);
   // One barrier pair per stage for both operands: the token-tile loader
   // arrives (with its bytes) on the A slot's ready barrier, and reuses B slot

@@ -160,8 +160,8 @@ def mxfp4_int8_moe_gemm_swiglu(a_q, a_scale, b_mxfp4, b_shift2, b_channel_scale,
 # ---- expert-sorted row pipeline (B200 fast path; same arithmetic) ----
 
 def _sorted_bm(block_m: int) -> int:
-    """The sorted-row GEMMs also take 256-token tiles; validate the rest as usual."""
-    return 128 if block_m == 256 else block_m
+    """The sorted-row GEMMs also take 192- and 256-token tiles; validate the rest as usual."""
+    return 128 if block_m in (192, 256) else block_m
 
 
 def moe_sort_rows(a_q, a_scale, sorted_token_ids, num_tokens_post_padded, *, topk: int,

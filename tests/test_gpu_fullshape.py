@@ -172,13 +172,13 @@ def test_decode_layer_full_shape_uniform(weights):
 
 def test_prefill_layer_full_shape_zipf(weights):
     r = _run_layer_stages(weights, 8192, "zipf", 1200)
-    assert r["bm"] == 256
+    assert r["bm"] in (192, 256)
     assert int(r["counts"].max()) > 1000
 
 
 def test_prefill_layer_full_shape_uniform(weights):
     r = _run_layer_stages(weights, 8192, "uniform", 1300)
-    assert r["bm"] == 256
+    assert r["bm"] in (192, 256)
     assert int((r["counts"] > 0).sum()) == E
 
 

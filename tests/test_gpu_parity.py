@@ -207,7 +207,10 @@ def _cm_rows(t, cap, k):  # K-chunk-major [k/128][cap][128] -> [cap][k]
 
 # the sorted path also runs 256-token tiles (N=256 MMAs, one issuer)
 SORTED_CASES = MOE_CASES + [(8, 1200, 256, 256, 2, 256), (4, 640, 1024, 256, 4, 256),
-                            (16, 300, 512, 128, 8, 256), (4, 600, 4352, 128, 2, 256)]
+                            (16, 300, 512, 128, 8, 256), (4, 600, 4352, 128, 2, 256),
+                            # 192-token tiles (two accumulators, 2-slot A ring)
+                            (8, 1200, 256, 256, 2, 192), (4, 600, 4352, 128, 2, 192),
+                            (16, 300, 512, 128, 8, 192)]
 
 
 @pytest.mark.parametrize("case", SORTED_CASES)
