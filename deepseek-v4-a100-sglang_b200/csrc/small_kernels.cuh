@@ -220,7 +220,20 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
     if (src >= a_rows) continue;
     const int4* row = reinterpret_cast<const int4*>(a + src * lda);
     int sum = 0;
-    for (int c = lane; c < nv; c += 32) {
+    // four 16-byte loads in flight per lane
+    int c = lane;
+    for (; c + 96 < nv; c += 128) {
+      int4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldg(row + c + 32 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int cc = c + 32 * u;
+        *reinterpret_cast<int4*>(out + (cc >> 3) * cap * 128 + pos * 128 + (cc & 7) * 16) = v[u];
+        sum = __dp4a(v[u].x, 0x01010101, __dp4a(v[u].y, 0x01010101, __dp4a(v[u].z, 0x01010101, __dp4a(v[u].w, 0x01010101, sum))));
+      }
+    }
+    for (; c < nv; c += 32) {
       const int4 v = __ldg(row + c);
       *reinterpret_cast<int4*>(out + (c >> 3) * cap * 128 + pos * 128 + (c & 7) * 16) = v;
       sum = __dp4a(v.x, 0x01010101, __dp4a(v.y, 0x01010101, __dp4a(v.z, 0x01010101, __dp4a(v.w, 0x01010101, sum))));
