@@ -10,7 +10,11 @@ import ctypes
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).with_name("libdsv4_b200.so")
+import os
+
+# DSV4_B200_LIB points at another build of the same library (A/B runs of
+# build variants); the in-tree build otherwise.
+LIB_PATH = Path(os.environ.get("DSV4_B200_LIB") or Path(__file__).with_name("libdsv4_b200.so"))
 
 DSV4_OK = 0
 DSV4_ERR_INVALID_ARGUMENT = 1
