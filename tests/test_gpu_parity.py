@@ -415,3 +415,36 @@ def test_ep_dispatch_pack_matches_torch_plan(world, m):
     got = buf.cpu()
     np.testing.assert_array_equal(pos.cpu().numpy(), plan.pos.numpy())
     np.testing.assert_array_equal(got[:, :h + 4 * w].numpy(), ref[:, :h + 4 * w].numpy())
+
+
+def test_moe_closer_to_mxfp4_than_rowwise_int4():
+    """TEST_MOE:261-310: prepare_mxfp4_int8_moe frees the original MXFP4
+    parameters, and the layer's error against the float MXFP4 MoE is below
+    0.08 and below that of a row-wise INT4 copy of the same weights."""
+    class Layer(torch.nn.Module):
+        pass
+
+    e, t, h, i, topk = 4, 17, 128, 128, 2
+    w13, s13 = G.make_random_packed_mxfp4(e, 2 * i, h, 11)
+    w2, s2 = G.make_random_packed_mxfp4(e, h, i, 12)
+    layer = Layer()
+    for nm, v in (("w13_weight", w13), ("w2_weight", w2), ("w13_weight_scale_inv", s13),
+                  ("w2_weight_scale_inv", s2)):
+        setattr(layer, nm, torch.nn.Parameter(v.to(DEV), requires_grad=False))
+    D.prepare_mxfp4_int8_moe(layer, headroom_bits=3, topk=topk)
+    for nm in ("w13_weight", "w2_weight", "w13_weight_scale_inv", "w2_weight_scale_inv"):
+        assert getattr(layer, nm).numel() == 0
+    x = G.randn_bf16((t, h), 20260618, 0.2)
+    ar = torch.arange(t, dtype=torch.int32)
+    ids = torch.stack([ar % e, (ar * 3 + 1) % e], dim=1)
+    gen = torch.Generator()
+    gen.manual_seed(5)
+    tw = torch.softmax(torch.randn(t, topk, generator=gen), dim=-1)
+    out = D.mxfp4_int8_moe_forward(x.to(DEV), layer._dsv4_mxfp4_int8_weights, ids.to(DEV),
+                                   tw.to(DEV), hidden_size=h, intermediate_size=i)
+    ref = O.mxfp4_moe_reference_torch(x, w13, s13, w2, s2, ids, tw).float().numpy()
+    int4 = O.int4_rowwise_moe_reference_torch(x, w13, s13, w2, s2, ids, tw).float().numpy()
+    int8_rel = O.relative_l2(out.float().cpu().numpy(), ref)
+    int4_rel = O.relative_l2(int4, ref)
+    assert int8_rel < 0.08
+    assert int8_rel < int4_rel
