@@ -165,15 +165,20 @@ class Layer:
     def __call__(self, x, ids, tw, record=False):
         import torch
         import dsv4_b200.jit_ops as J
+        import dsv4_b200.mxfp4_int8_moe as MM
         D, w, m = self.D, self.w, self.m
         kw = dict(hidden_size=H, intermediate_size=I, topk=TOPK, block_m=self.bm,
                   num_valid_tokens=m * TOPK)
-        s, e, n = D.moe_align_block_size(ids, self.bm, E)
-        if m <= 512:  # as mxfp4_int8_moe_forward: one quantise + sort launch at decode
+        # as mxfp4_int8_moe_forward: each token quantised once and scattered
+        # through the align's inverse map (by sorted position up to the
+        # library's threshold, 0 tokens by default)
+        if m <= MM._FUSED_QUANT_SORT_MAX_TOKENS:
+            s, e, n = D.moe_align_block_size(ids, self.bm, E)
             a13, s13, r13 = J.quantize_sort_int8(x, s, n, topk=TOPK, num_valid_tokens=m * TOPK)
         else:
-            q, qs = D.quantize_per_token_int8(x)
-            a13, s13, r13 = J.moe_sort_rows(q, qs, s, n, topk=TOPK, num_valid_tokens=m * TOPK)
+            s, e, n, spos = D.moe_align_block_size(ids, self.bm, E, return_slot_pos=True)
+            a13, s13, r13 = J.quantize_scatter_int8(x, spos, s.numel(), topk=TOPK,
+                                                    num_valid_tokens=m * TOPK)
         inter = torch.empty((s.numel(), I), device=self.dev, dtype=torch.bfloat16)
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
         if record:
@@ -200,7 +205,7 @@ class Layer:
         return statistics.mean(w13), statistics.mean(w2)
 
 
-LAUNCHES_PER_STEP = 6  # decode: align, quant+sort, W13+SwiGLU, quant, W2, combine
+LAUNCHES_PER_STEP = 6  # align, quant+sort (or quant+scatter), W13+SwiGLU, quant, W2, combine
 
 
 MODEL_SEED = 7  # router bias and expert popularity: properties of the model, shared by all ranks

@@ -668,7 +668,7 @@ int dsv4_b200_router_align(const void* logits, int dtype, int64_t m, int64_t num
                            int32_t* sorted_token_ids, int64_t sorted_capacity,
                            int32_t* expert_ids, int64_t expert_ids_capacity,
                            int32_t* num_tokens_post_pad, int32_t* workspace,
-                           int64_t workspace_words, void* stream) {
+                           int64_t workspace_words, int32_t* slot_pos, void* stream) {
   if (int r = ensure_init()) return r;
   DSV4_REQUIRE(m >= 0 && m < (1ll << 27), "bad m %lld", (long long)m);
   DSV4_REQUIRE(num_experts >= 1 && num_experts <= kAlignMaxExperts,
@@ -694,7 +694,7 @@ int dsv4_b200_router_align(const void* logits, int dtype, int64_t m, int64_t num
   int cap_i = static_cast<int>(sorted_capacity), ecap_i = static_cast<int>(expert_ids_capacity);
   void* args[] = {&logits, &m_i, &e_i, &bias, &k_i, &renormalize, &scale, &bm_i, &tpc,
                   &topk_ids, &topk_weights, &sorted_token_ids, &cap_i, &expert_ids, &ecap_i,
-                  &num_tokens_post_pad, &workspace};
+                  &num_tokens_post_pad, &workspace, &slot_pos};
   const void* fn = router_align_fn(dtype, epl);
   if (fn == nullptr)
     return fail(DSV4_ERR_INVALID_ARGUMENT, "logits must be fp32, fp16, or bf16 (dtype %d)", dtype);
@@ -730,7 +730,8 @@ int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int64
   launch_pdl(&moe_align_kernel, 1, kAlignThreads, smem, as_stream(stream), 
       topk_ids, static_cast<int>(numel), static_cast<int>(num_experts),
       static_cast<int>(block_size), sorted_token_ids, static_cast<int>(sorted_capacity),
-      expert_ids, static_cast<int>(expert_ids_capacity), num_tokens_post_pad, cumsum_buffer);
+      expert_ids, static_cast<int>(expert_ids_capacity), num_tokens_post_pad, cumsum_buffer,
+      static_cast<int32_t*>(nullptr));
   return check_launch("moe_align_kernel");
 }
 
@@ -747,7 +748,7 @@ int dsv4_b200_moe_align_block_size_ws(const int32_t* topk_ids, int64_t numel,
                                       int32_t* expert_ids, int64_t expert_ids_capacity,
                                       int32_t* num_tokens_post_pad, int32_t* cumsum_buffer,
                                       int32_t* workspace, int64_t workspace_words,
-                                      void* stream) {
+                                      int32_t* slot_pos, void* stream) {
   if (int r = ensure_init()) return r;
   DSV4_REQUIRE(num_experts >= 1 && num_experts <= kAlignMaxExperts,
                "num_experts must be in [1, %d], got %lld", kAlignMaxExperts,
@@ -770,7 +771,8 @@ int dsv4_b200_moe_align_block_size_ws(const int32_t* topk_ids, int64_t numel,
   int bm_i = static_cast<int>(block_size), ipc = static_cast<int>((numel + grid - 1) / grid);
   int cap_i = static_cast<int>(sorted_capacity), ecap_i = static_cast<int>(expert_ids_capacity);
   void* args[] = {&topk_ids, &numel_i, &e_i, &bm_i, &ipc, &sorted_token_ids, &cap_i,
-                  &expert_ids, &ecap_i, &num_tokens_post_pad, &cumsum_buffer, &workspace};
+                  &expert_ids, &ecap_i, &num_tokens_post_pad, &cumsum_buffer, &workspace,
+                  &slot_pos};
   cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&moe_align_coop_kernel),
                                               dim3(static_cast<unsigned>(grid)),
                                               dim3(kRouteAlignThreads), args,
@@ -911,6 +913,42 @@ int dsv4_b200_quantize_sort_int8(const void* a, int dtype, int64_t m_in, int64_t
   }
 #undef DSV4_QG
   return check_launch("quant_rows_reg_kernel (quantise + sort)");
+}
+
+int dsv4_b200_quantize_scatter_int8(const void* a, int dtype, int64_t m_in, int64_t k,
+                                    const int32_t* slot_pos, int64_t topk,
+                                    int64_t num_valid_tokens, int64_t sorted_capacity,
+                                    int8_t* out_q, float* out_scale, int32_t* out_rowsum,
+                                    void* stream) {
+  if (int r = ensure_init()) return r;
+  DSV4_REQUIRE(dtype == DSV4_BF16 || dtype == DSV4_F16, "a must be bf16 or fp16 (dtype %d)", dtype);
+  DSV4_REQUIRE(k > 0 && k % 128 == 0 && k <= 8192, "K must be a multiple of 128 in [128, 8192]");
+  DSV4_REQUIRE(topk >= 1 && topk <= 32, "topk must be in [1, 32], got %lld", (long long)topk);
+  DSV4_REQUIRE(m_in >= 0 && m_in < (1ll << 27) && num_valid_tokens >= 0 &&
+                   num_valid_tokens <= m_in * topk,
+               "token rows do not cover num_valid_tokens");
+  DSV4_REQUIRE(sorted_capacity >= 0 && sorted_capacity < (1ll << 31), "bad sorted_capacity");
+  if (sorted_capacity == 0 || m_in == 0 || num_valid_tokens == 0) return DSV4_OK;
+  DSV4_REQUIRE(a && slot_pos && out_q && out_scale && out_rowsum, "null pointer argument");
+  DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out_q) & 7) == 0,
+               "a must be 16-byte and out_q 8-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const bool wide = k > 2048;
+  const int rows_per_cta = wide ? 2 : 8;
+  const dim3 g(static_cast<unsigned>((m_in + rows_per_cta - 1) / rows_per_cta));
+  const int nv = static_cast<int>(num_valid_tokens);
+  const int tk = static_cast<int>(topk);
+#define DSV4_QSC(T, RT)                                                                       \
+  launch_pdl(&quant_scatter_kernel<T, RT, 8>, g, 256, 0, st, static_cast<const T*>(a), m_in, k, \
+             k, slot_pos, tk, nv, sorted_capacity, out_q, out_scale, out_rowsum)
+  if (dtype == DSV4_BF16) {
+    if (wide) DSV4_QSC(__nv_bfloat16, 128); else DSV4_QSC(__nv_bfloat16, 32);
+  } else {
+    if (wide) DSV4_QSC(__half, 128); else DSV4_QSC(__half, 32);
+  }
+#undef DSV4_QSC
+  return check_launch("quant_scatter_kernel");
 }
 
 int dsv4_b200_mxfp4_int8_moe_gemm_sorted(

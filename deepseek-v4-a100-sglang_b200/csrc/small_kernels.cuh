@@ -247,6 +247,107 @@ __global__ void __launch_bounds__(256) sort_rows_kernel(const int8_t* __restrict
   }
 }
 
+// Quantise + scatter into expert order: the inverse of the fused quantise +
+// sort.  Each token row is read and quantised once (the arithmetic of
+// quant_rows_kernel), and its int8 values, scale and int8 row sum are written
+// to the sorted position of each of its topk routed slots, K-chunk-major
+// [K/128][cap][128]: slot_pos[t * topk + j] (-1: not placed).  Slots at or
+// past num_valid are skipped.  The outputs equal quantise-then-sort_rows bit
+// for bit; padding positions are left unwritten.  RT threads per row,
+// 256 / RT rows per CTA, VPT 16-byte loads per thread (K <= 8 RT VPT).
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(256) quant_scatter_kernel(const T* __restrict__ a, int64_t m,
+                                                            int64_t k, int64_t lda,
+                                                            const int32_t* __restrict__ slot_pos,
+                                                            int topk, int num_valid, int64_t cap,
+                                                            int8_t* __restrict__ q,
+                                                            float* __restrict__ scale,
+                                                            int32_t* __restrict__ rowsum) {
+  pdl_entry();
+  constexpr int kRowsPerCta = 256 / RT;
+  __shared__ float red[256 / 32];
+  __shared__ int red_i[256 / 32];
+  const int r_local = threadIdx.x / RT;
+  const int lt = threadIdx.x % RT;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerCta + r_local;
+  const bool active = row < m;
+  const int nv = static_cast<int>(k / 8);
+  uint4 u[VPT];
+  float amax = 0.f;
+  if (active) {
+    const uint4* xv = reinterpret_cast<const uint4*>(a + row * lda);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = lt + i * RT;
+      if (idx < nv) {
+        u[i] = __ldg(xv + idx);
+        const T* e = reinterpret_cast<const T*>(&u[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(to_f32<T>(e[j])));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (RT > 32) {
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    const int w0 = (r_local * RT) >> 5;
+    amax = 0.f;
+#pragma unroll
+    for (int w = 0; w < RT / 32; ++w) amax = fmaxf(amax, red[w0 + w]);
+  }
+  float sc = __fdiv_rn(amax, 127.0f);
+  if (sc == 0.0f) sc = 1.0f;
+  uint2 packed[VPT];
+  int qsum = 0;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = lt + i * RT;
+    packed[i] = make_uint2(0u, 0u);
+    if (active && idx < nv) {
+      const T* e = reinterpret_cast<const T*>(&u[i]);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(to_f32<T>(e[j]), sc))) << (8 * j);
+        hi |= static_cast<uint32_t>(static_cast<uint8_t>(quant1(to_f32<T>(e[j + 4]), sc))) << (8 * j);
+      }
+      packed[i] = make_uint2(lo, hi);
+      qsum = __dp4a(static_cast<int>(lo), 0x01010101, qsum);
+      qsum = __dp4a(static_cast<int>(hi), 0x01010101, qsum);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+  if (RT > 32) {
+    if ((threadIdx.x & 31) == 0) red_i[threadIdx.x >> 5] = qsum;
+    __syncthreads();
+    const int w0 = (r_local * RT) >> 5;
+    qsum = 0;
+#pragma unroll
+    for (int w = 0; w < RT / 32; ++w) qsum += red_i[w0 + w];
+  }
+  if (!active) return;
+  for (int j = 0; j < topk; ++j) {
+    const int64_t slot = row * topk + j;
+    if (slot >= num_valid) break;
+    const int pos = __ldg(slot_pos + slot);
+    if (pos < 0 || pos >= cap) continue;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = lt + i * RT;
+      if (idx < nv)
+        *reinterpret_cast<uint2*>(q + (idx >> 4) * cap * 128 + static_cast<int64_t>(pos) * 128 +
+                                  (idx & 15) * 8) = packed[i];
+    }
+    if (lt == 0) {
+      scale[pos] = sc;
+      rowsum[pos] = qsum;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Router top-k (the DeepSeek routing SGLang computes before the MoE call,
 // reference PATCH:505-507): score = sigmoid(logit); the top-k experts by
@@ -334,14 +435,16 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const T* __restrict__ 
 //      groups equal experts, the rank among lower lanes gives the position.
 // Result: inside an expert segment slot ids increase (stable order); padding
 // value is numel; ids outside [0, E) are dropped; expert_ids of blocks past
-// the padded total are -1.
+// the padded total are -1.  Optionally slot_pos[i] = the position of slot i
+// (-1 for a dropped id): the inverse permutation, for the quantise-scatter.
 // ---------------------------------------------------------------------------
 constexpr int kAlignThreads = 1024;
 
 __global__ void __launch_bounds__(kAlignThreads, 1)
 moe_align_kernel(const int32_t* __restrict__ ids, int numel, int num_experts, int block_m,
                  int32_t* __restrict__ sorted_ids, int sorted_cap, int32_t* __restrict__ expert_ids,
-                 int expert_cap, int32_t* __restrict__ ntpp, int32_t* __restrict__ cumsum_out) {
+                 int expert_cap, int32_t* __restrict__ ntpp, int32_t* __restrict__ cumsum_out,
+                 int32_t* __restrict__ slot_pos) {
   pdl_entry();
   extern __shared__ int sm_align[];
   const int E = num_experts;
@@ -428,10 +531,12 @@ moe_align_kernel(const int32_t* __restrict__ ids, int numel, int num_experts, in
     const int key = valid ? e : (E + lane);  // unique key for invalid lanes
     const unsigned peers = __match_any_sync(0xffffffffu, key);
     const int rank = __popc(peers & lt_mask);
+    int pos = -1;
     if (valid) {
-      const int pos = base[e] + wc[warp * E + e] + rank;
-      if (pos < sorted_cap) sorted_ids[pos] = i;
+      pos = base[e] + wc[warp * E + e] + rank;
+      if (pos < sorted_cap) sorted_ids[pos] = i; else pos = -1;
     }
+    if (slot_pos != nullptr && i < s_end) slot_pos[i] = pos;
     __syncwarp();
     if (valid && rank == 0) wc[warp * E + e] += __popc(peers);
     __syncwarp();
@@ -772,7 +877,8 @@ router_align_kernel(const T* __restrict__ logits, int m, int num_experts,
                     int block_m, int tpc, int32_t* __restrict__ topk_ids,
                     float* __restrict__ topk_weights, int32_t* __restrict__ sorted_ids,
                     int sorted_cap, int32_t* __restrict__ expert_ids, int expert_cap,
-                    int32_t* __restrict__ ntpp, int32_t* __restrict__ cta_counts) {
+                    int32_t* __restrict__ ntpp, int32_t* __restrict__ cta_counts,
+                    int32_t* __restrict__ slot_pos) {
   extern __shared__ int sm_ra[];
   const int E = num_experts;
   int* wc = sm_ra;             // [32][E] per-warp counts, then per-warp cursors
@@ -871,6 +977,7 @@ router_align_kernel(const T* __restrict__ logits, int m, int num_experts,
       const int e = topk_ids[static_cast<int64_t>(t) * topk + lane];
       const int pos = ebase[e] + cbase[e] + wc[warp * E + e];
       if (pos < sorted_cap) sorted_ids[pos] = t * topk + lane;
+      if (slot_pos != nullptr) slot_pos[t * topk + lane] = pos < sorted_cap ? pos : -1;
       wc[warp * E + e] += 1;
     }
     __syncwarp();
@@ -895,7 +1002,7 @@ moe_align_coop_kernel(const int32_t* __restrict__ ids, int numel, int num_expert
                       int ipc, int32_t* __restrict__ sorted_ids, int sorted_cap,
                       int32_t* __restrict__ expert_ids, int expert_cap,
                       int32_t* __restrict__ ntpp, int32_t* __restrict__ cumsum_out,
-                      int32_t* __restrict__ cta_counts) {
+                      int32_t* __restrict__ cta_counts, int32_t* __restrict__ slot_pos) {
   extern __shared__ int sm_ac[];
   const int E = num_experts;
   int* wc = sm_ac;
@@ -990,10 +1097,12 @@ moe_align_coop_kernel(const int32_t* __restrict__ ids, int numel, int num_expert
     const int key = valid ? e : (E + lane);  // unique key for invalid lanes
     const unsigned peers = __match_any_sync(0xffffffffu, key);
     const int rank = __popc(peers & lt_mask);
+    int pos = -1;
     if (valid) {
-      const int pos = ebase[e] + cbase[e] + wc[warp * E + e] + rank;
-      if (pos < sorted_cap) sorted_ids[pos] = i;
+      pos = ebase[e] + cbase[e] + wc[warp * E + e] + rank;
+      if (pos < sorted_cap) sorted_ids[pos] = i; else pos = -1;
     }
+    if (slot_pos != nullptr && i < w_end) slot_pos[i] = pos;
     __syncwarp();
     if (valid && rank == 0) wc[warp * E + e] += __popc(peers);
     __syncwarp();

@@ -28,6 +28,7 @@ from .jit_ops import (  # noqa: F401
     mxfp4_int8_moe_gemm_swiglu,
     mxfp4_int8_moe_reduce,
     moe_sort_rows,
+    quantize_scatter_int8,
     quantize_sorted_int8,
     mxfp4_int8_moe_gemm_sorted,
     mxfp4_int8_moe_gemm_swiglu_sorted,

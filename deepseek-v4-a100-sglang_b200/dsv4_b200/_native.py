@@ -39,10 +39,10 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_remap_mxfp4_weight_for_int8": [_P, _P, _I64, _I64, _I64, _I, _I, _P, _P, _P, _P],
     "dsv4_b200_router_align_workspace_words": [_I64, _I64, _P],
     "dsv4_b200_router_align": [_P, _I, _I64, _I64, _P, _I64, _I, _F, _I64, _P, _P, _P, _I64, _P,
-                               _I64, _P, _P, _I64, _P],
+                               _I64, _P, _P, _I64, _P, _P],
     "dsv4_b200_moe_align_workspace_words": [_I64, _I64, _P],
     "dsv4_b200_moe_align_block_size_ws": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P,
-                                          _I64, _P],
+                                          _I64, _P, _P],
     "dsv4_b200_moe_align_block_size": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P],
     "dsv4_b200_mxfp4_int8_moe_gemm": [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P,
                                       _I64, _P, _I64, _P, _I64, _I64, _I, _I64, _P],
@@ -53,6 +53,7 @@ SIGNATURES: dict[str, list] = {
     "dsv4_b200_moe_sort_rows": [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I, _I64, _P, _P, _P,
                                 _P],
     "dsv4_b200_quantize_sort_int8": [_P, _I, _I64, _I64, _P, _I64, _P, _I64, _I64, _P, _P, _P, _P],
+    "dsv4_b200_quantize_scatter_int8": [_P, _I, _I64, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _P],
     "dsv4_b200_quantize_sorted_int8": [_P, _I, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P],
     "dsv4_b200_mxfp4_int8_moe_gemm_sorted": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
                                              _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P],

@@ -214,6 +214,32 @@ def quantize_sort_int8(a, sorted_token_ids, num_tokens_post_padded, *, topk: int
     return q, sc, rs
 
 
+def quantize_scatter_int8(a, slot_pos, sorted_capacity: int, *, topk: int,
+                          num_valid_tokens: int):
+    """Same outputs as :func:`quantize_sort_int8`, computed from the token
+    side: each row of ``a`` [M, K] is quantised once and written to the sorted
+    position ``slot_pos[t * topk + j]`` of each routed slot (``slot_pos`` from
+    :func:`moe_align_block_size` / :func:`router_align` with
+    ``return_slot_pos=True``).  For many tokens, where quantising every routed
+    copy again would cost topk times the arithmetic."""
+    _check(a.dim() == 2 and a.dtype in (torch.bfloat16, torch.float16) and a.is_contiguous(),
+           "a must be a contiguous 2-D bf16/fp16 tensor")
+    _check(a.is_cuda, "a must be a CUDA tensor (no CPU path)")
+    m, k = a.shape
+    _check(slot_pos.dtype == torch.int32 and slot_pos.is_contiguous() and
+           slot_pos.numel() >= num_valid_tokens, "slot_pos must be int32 [>= num_valid_tokens]")
+    cap = int(sorted_capacity)
+    q = torch.empty(cap * k, device=a.device, dtype=torch.int8)
+    sc = torch.empty(cap, device=a.device, dtype=torch.float32)
+    rs = torch.empty(cap, device=a.device, dtype=torch.int32)
+    _init_device(a.device)
+    N.call("dsv4_b200_quantize_scatter_int8", a.data_ptr(),
+           N.DTYPE_BF16 if a.dtype == torch.bfloat16 else N.DTYPE_F16, m, k,
+           slot_pos.data_ptr(), topk, num_valid_tokens, cap, q.data_ptr(), sc.data_ptr(),
+           rs.data_ptr(), N.stream_of(a))
+    return q, sc, rs
+
+
 def quantize_sorted_int8(a, sorted_token_ids, num_tokens_post_padded, *, num_valid_tokens: int):
     """Per-token INT8 quantisation of sorted-position rows ``a``
     ``[sorted_capacity, K]`` (bf16/fp16) into ``(q, scale, rowsum)`` as

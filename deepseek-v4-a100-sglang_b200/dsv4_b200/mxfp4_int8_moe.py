@@ -23,6 +23,7 @@ from .jit_ops import (
     mxfp4_int8_dense_gemm,
     prewarm_mxfp4_int8_moe_jit_modules,
     moe_sort_rows,
+    quantize_scatter_int8,
     quantize_sort_int8,
     quantize_sorted_int8,
     mxfp4_int8_moe_gemm_swiglu_sorted,
@@ -270,11 +271,12 @@ def router_topk(router_logits: torch.Tensor, topk: int, *, bias: torch.Tensor | 
 
 def router_align(router_logits: torch.Tensor, topk: int, block_size: int, *,
                  bias: torch.Tensor | None = None, renormalize: bool = True,
-                 scale: float = 1.0):
+                 scale: float = 1.0, return_slot_pos: bool = False):
     """:func:`router_topk` and :func:`moe_align_block_size` in one launch
     (a cooperative kernel; same results bit for bit).  Returns
     ``(topk_ids, topk_weights, sorted_token_ids, expert_ids,
-    num_tokens_post_pad)``."""
+    num_tokens_post_pad)``, plus ``slot_pos`` (the sorted position of each
+    routed slot) with ``return_slot_pos``."""
     if router_logits.dim() != 2 or router_logits.dtype not in _DTYPES:
         raise ValueError("router_logits must be a 2-D fp32/fp16/bf16 tensor")
     _require_cuda(router_logits, "router_logits")
@@ -297,11 +299,15 @@ def router_align(router_logits: torch.Tensor, topk: int, block_size: int, *,
     words = ctypes.c_int64(0)
     N.call("dsv4_b200_router_align_workspace_words", m, e, ctypes.byref(words))
     ws = torch.empty((max(words.value, 1),), dtype=torch.int32, device=dev)
+    slot_pos = (torch.empty((m * topk,), dtype=torch.int32, device=dev)
+                if return_slot_pos else None)
     N.call("dsv4_b200_router_align", logits.data_ptr(), _DTYPES[logits.dtype], m, e,
            b.data_ptr() if b is not None else None, topk, 1 if renormalize else 0, float(scale),
            block_size, ids.data_ptr(), w.data_ptr(), sorted_ids.data_ptr(), cap,
            expert_ids.data_ptr(), n_blocks, ntpp.data_ptr(), ws.data_ptr(), ws.numel(),
-           N.stream_of(logits))
+           slot_pos.data_ptr() if slot_pos is not None else None, N.stream_of(logits))
+    if return_slot_pos:
+        return ids, w, sorted_ids, expert_ids, ntpp, slot_pos
     return ids, w, sorted_ids, expert_ids, ntpp
 
 
@@ -312,10 +318,13 @@ def align_capacity(numel: int, num_experts: int, block_size: int) -> int:
     return numel + (num_experts + 1) * (block_size - 1)
 
 
-def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int):
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int, *,
+                         return_slot_pos: bool = False):
     """Native replacement of ``_moe_align_block_size`` (PYMOE:842-869):
     ``(sorted_token_ids, expert_ids, num_tokens_post_pad)``.  Stable order
-    inside each expert; padding value ``numel``; ids outside [0, E) dropped."""
+    inside each expert; padding value ``numel``; ids outside [0, E) dropped.
+    With ``return_slot_pos`` a fourth tensor, int32 ``[numel]``: the sorted
+    position of each id (-1 when dropped), the inverse permutation."""
     _require_cuda(topk_ids, "topk_ids")
     ids = topk_ids.to(torch.int32).contiguous()
     numel = ids.numel()
@@ -325,15 +334,21 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
     n_blocks = (cap + block_size - 1) // block_size
     expert_ids = torch.empty((n_blocks,), dtype=torch.int32, device=dev)
     ntpp = torch.empty((1,), dtype=torch.int32, device=dev)
-    if numel >= _ALIGN_COOP_MIN_IDS:
-        # many ids: the multi-CTA align (same outputs)
+    if numel >= _ALIGN_COOP_MIN_IDS or return_slot_pos:
+        # many ids: the multi-CTA align (same outputs); it also records the
+        # inverse permutation
         import ctypes
         words = ctypes.c_int64(0)
         N.call("dsv4_b200_moe_align_workspace_words", numel, num_experts, ctypes.byref(words))
         ws = torch.empty((max(words.value, 1),), dtype=torch.int32, device=dev)
-        N.call("dsv4_b200_moe_align_block_size_ws", ids.data_ptr(), numel, num_experts,
-               block_size, sorted_ids.data_ptr(), cap, expert_ids.data_ptr(), n_blocks,
-               ntpp.data_ptr(), None, ws.data_ptr(), ws.numel(), N.stream_of(ids))
+        slot_pos = (torch.empty((max(numel, 1),), dtype=torch.int32, device=dev)
+                    if return_slot_pos else None)
+        N.call("dsv4_b200_moe_align_block_size_ws", ids.data_ptr() if numel else None, numel,
+               num_experts, block_size, sorted_ids.data_ptr(), cap, expert_ids.data_ptr(),
+               n_blocks, ntpp.data_ptr(), None, ws.data_ptr(), ws.numel(),
+               slot_pos.data_ptr() if slot_pos is not None else None, N.stream_of(ids))
+        if return_slot_pos:
+            return sorted_ids, expert_ids, ntpp, slot_pos[:numel]
         return sorted_ids, expert_ids, ntpp
     N.call("dsv4_b200_moe_align_block_size", ids.data_ptr() if numel else None, numel, num_experts,
            block_size, sorted_ids.data_ptr(), cap, expert_ids.data_ptr(), n_blocks,
@@ -341,8 +356,12 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
     return sorted_ids, expert_ids, ntpp
 
 
-# tokens up to which the layer quantises and sorts in one launch
-_FUSED_QUANT_SORT_MAX_TOKENS = 512
+# tokens up to which the layer quantises by sorted position (every routed
+# copy quantised again); above it each token is quantised once and scattered
+# through the align's inverse map.  The scatter measured faster at every M
+# from 16 to 8192 on B200 (12.2 vs 14.2 us at M=16, 117 vs 566 us at 8192),
+# so the per-position form is left to explicit callers.
+_FUSED_QUANT_SORT_MAX_TOKENS = 0
 
 # ids from which moe_align_block_size runs the multi-CTA kernel
 _ALIGN_COOP_MIN_IDS = 8192
@@ -373,12 +392,17 @@ def mxfp4_int8_moe_forward(hidden_states: torch.Tensor, weights: Mxfp4Int8MoeWei
     experts = weights.w13_mxfp4.shape[0]
     _, block_n = _select_moe_tile_shape(m, topk, experts)
     block_m = select_sorted_block_m(m, topk, experts)
-    sorted_ids, expert_ids, ntpp = moe_align_block_size(topk_ids_i32, block_m, experts)
+    slot_pos = None
+    if m > _FUSED_QUANT_SORT_MAX_TOKENS:
+        sorted_ids, expert_ids, ntpp, slot_pos = moe_align_block_size(
+            topk_ids_i32, block_m, experts, return_slot_pos=True)
+    else:
+        sorted_ids, expert_ids, ntpp = moe_align_block_size(topk_ids_i32, block_m, experts)
     return _moe_core(None, None, weights, topk_ids_i32, topk_weights_f32, sorted_ids,
                      expert_ids, ntpp, block_m=block_m, block_n=block_n, hidden_size=hidden_size,
                      intermediate_size=intermediate_size,
                      routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
-                     masked=False, hidden=hidden_states)
+                     masked=False, hidden=hidden_states, slot_pos=slot_pos)
 
 
 def mxfp4_int8_moe_forward_from_logits(hidden_states: torch.Tensor,
@@ -400,19 +424,21 @@ def mxfp4_int8_moe_forward_from_logits(hidden_states: torch.Tensor,
     experts = weights.w13_mxfp4.shape[0]
     _, block_n = _select_moe_tile_shape(m, topk, experts)
     block_m = select_sorted_block_m(m, topk, experts)
-    ids, w, sorted_ids, expert_ids, ntpp = router_align(router_logits, topk, block_m,
-                                                        bias=router_bias, renormalize=renormalize)
+    scatter = m > _FUSED_QUANT_SORT_MAX_TOKENS
+    ids, w, sorted_ids, expert_ids, ntpp, *rest = router_align(
+        router_logits, topk, block_m, bias=router_bias, renormalize=renormalize,
+        return_slot_pos=scatter)
     out = _moe_core(None, None, weights, ids, w, sorted_ids, expert_ids, ntpp,
                     block_m=block_m, block_n=block_n, hidden_size=hidden_size,
                     intermediate_size=intermediate_size,
                     routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
-                    masked=False, hidden=hidden_states)
+                    masked=False, hidden=hidden_states, slot_pos=rest[0] if rest else None)
     return out, ids, w
 
 
 def _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_ids, expert_ids,
               ntpp, *, block_m, block_n, hidden_size, intermediate_size, routed_scaling_factor,
-              clamp_limit, masked, hidden=None):
+              clamp_limit, masked, hidden=None, slot_pos=None):
     """W13 + SwiGLU, requantisation and W2 of mxfp4_int8_moe_forward
     (PYMOE:904-958) on expert-sorted rows: the routed token rows are copied
     once into the order of the aligned permutation (K-chunk-major), so each
@@ -429,6 +455,11 @@ def _moe_core(a13_q, a13_scale, weights, topk_ids_i32, topk_weights_f32, sorted_
         # token is quantised again; cheap at decode, not at prefill)
         a13, s13, r13 = quantize_sort_int8(hidden, sorted_ids, ntpp, topk=topk,
                                            num_valid_tokens=nv)
+    elif hidden is not None and slot_pos is not None:
+        # many tokens: quantise each token once and scatter its routed copies
+        # to their sorted positions (the inverse map from the align)
+        a13, s13, r13 = quantize_scatter_int8(hidden, slot_pos, sorted_ids.numel(), topk=topk,
+                                              num_valid_tokens=nv)
     else:
         if hidden is not None:
             a13_q, a13_scale = quantize_per_token_int8(hidden, 0.0)

@@ -102,7 +102,9 @@ DSV4_API int dsv4_b200_router_topk(const void* logits, int dtype, int64_t m, int
  * expert_ids, num_tokens_post_pad.  `workspace` holds per-CTA expert counts:
  * at least the number of int32 words that
  * dsv4_b200_router_align_workspace_words(m, num_experts) reports; nothing in
- * it needs to start at zero.  num_experts <= 1024. */
+ * it needs to start at zero.  num_experts <= 1024.  slot_pos (NULL, or int32
+ * [m * topk]) receives the sorted position of each routed slot: the inverse
+ * of sorted_token_ids, for dsv4_b200_quantize_scatter_int8. */
 DSV4_API int dsv4_b200_router_align_workspace_words(int64_t m, int64_t num_experts,
                                                     int64_t* words);
 DSV4_API int dsv4_b200_router_align(const void* logits, int dtype, int64_t m,
@@ -112,7 +114,7 @@ DSV4_API int dsv4_b200_router_align(const void* logits, int dtype, int64_t m,
                                     int32_t* sorted_token_ids, int64_t sorted_capacity,
                                     int32_t* expert_ids, int64_t expert_ids_capacity,
                                     int32_t* num_tokens_post_pad, int32_t* workspace,
-                                    int64_t workspace_words, void* stream);
+                                    int64_t workspace_words, int32_t* slot_pos, void* stream);
 
 /* a5. Expert histogram + block-padded prefix sum + stable permutation.
  * Replaces the sgl_kernel.moe_align_block_size call of
@@ -130,7 +132,9 @@ DSV4_API int dsv4_b200_moe_align_block_size(const int32_t* topk_ids, int64_t num
  * same outputs bit for bit) for large inputs: the library's op uses it from
  * 8,192 ids up.  `workspace` holds per-CTA expert counts: at least the
  * int32 words dsv4_b200_moe_align_workspace_words(numel, num_experts)
- * reports; nothing in it needs to start at zero. */
+ * reports; nothing in it needs to start at zero.  slot_pos (NULL, or int32
+ * [numel]) receives the sorted position of each id (-1 for an id outside
+ * [0, E)). */
 DSV4_API int dsv4_b200_moe_align_workspace_words(int64_t numel, int64_t num_experts,
                                                  int64_t* words);
 DSV4_API int dsv4_b200_moe_align_block_size_ws(const int32_t* topk_ids, int64_t numel,
@@ -140,7 +144,8 @@ DSV4_API int dsv4_b200_moe_align_block_size_ws(const int32_t* topk_ids, int64_t 
                                                int64_t expert_ids_capacity,
                                                int32_t* num_tokens_post_pad,
                                                int32_t* cumsum_buffer, int32_t* workspace,
-                                               int64_t workspace_words, void* stream);
+                                               int64_t workspace_words, int32_t* slot_pos,
+                                               void* stream);
 
 /* a6/a8. Grouped MXFP4 x INT8 GEMM over the aligned permutation:
  *   dst[slot][n] = bf16((f32(sum_k a_q[src][k] * W[e][n][k]) * a_scale[src]) * cs[e][n])
@@ -203,9 +208,6 @@ DSV4_API int dsv4_b200_moe_sort_rows(const int8_t* a_q, const float* a_scale, in
                                      int8_t* out_q, float* out_scale, int32_t* out_rowsum,
                                      void* stream);
 
-/* Per-token INT8 quantisation (a1, PYMOE:46-66 arithmetic, no clamp) of the
- * sorted-position rows a [sorted_capacity][k] (bf16 or fp16), written
- * K-chunk-major.  The W2 input requantisation of PYMOE:937. */
 /* Per-token INT8 quantisation fused with the sort into expert order: the
  * quantiser of dsv4_b200_quantize_per_token_int8 (PYMOE:53-126) applied to
  * token row sorted_token_ids[p] / topk of `a` [m_in][k] (bf16/fp16) and
@@ -218,6 +220,21 @@ DSV4_API int dsv4_b200_quantize_sort_int8(const void* a, int dtype, int64_t m_in
                                           const int32_t* num_tokens_post_padded, int64_t topk,
                                           int64_t num_valid_tokens, int8_t* out_q,
                                           float* out_scale, int32_t* out_rowsum, void* stream);
+/* The same quantise-and-sort from the other side, for many tokens: each token
+ * row of `a` [m_in][k] is read and quantised once, and written (values,
+ * scale, row sum) to the sorted position slot_pos[t * topk + j] of each of
+ * its routed slots below num_valid_tokens (-1: skipped).  slot_pos comes
+ * from dsv4_b200_moe_align_block_size_ws or dsv4_b200_router_align.  Same
+ * outputs as dsv4_b200_quantize_sort_int8 bit for bit; padding positions are
+ * left unwritten. */
+DSV4_API int dsv4_b200_quantize_scatter_int8(const void* a, int dtype, int64_t m_in, int64_t k,
+                                             const int32_t* slot_pos, int64_t topk,
+                                             int64_t num_valid_tokens, int64_t sorted_capacity,
+                                             int8_t* out_q, float* out_scale,
+                                             int32_t* out_rowsum, void* stream);
+/* Per-token INT8 quantisation (a1, PYMOE:46-66 arithmetic, no clamp) of the
+ * sorted-position rows a [sorted_capacity][k] (bf16 or fp16), written
+ * K-chunk-major.  The W2 input requantisation of PYMOE:937. */
 DSV4_API int dsv4_b200_quantize_sorted_int8(const void* a, int dtype, int64_t k,
                                             const int32_t* sorted_token_ids,
                                             int64_t sorted_capacity,

@@ -105,6 +105,13 @@ def _run_layer_stages(weights, m, kind, seed):
     frows = fa13.view(H // 128, cap, 128).permute(1, 0, 2).reshape(cap, H)
     assert torch.equal(frows[valid], rows13[valid])
     assert torch.equal(fs13[valid], s13[valid]) and torch.equal(fr13[valid], r13[valid])
+    # and so does the quantise-scatter through the align's inverse map
+    s_b, e_b, n_b, spos = D.moe_align_block_size(ids.to(DEV), bm, E, return_slot_pos=True)
+    assert torch.equal(s_b, s) and torch.equal(e_b, e) and torch.equal(n_b, n)
+    ga13, gs13, gr13 = J.quantize_scatter_int8(xd, spos, cap, topk=TOPK, num_valid_tokens=nv)
+    grows = ga13.view(H // 128, cap, 128).permute(1, 0, 2).reshape(cap, H)
+    assert torch.equal(grows[valid], rows13[valid])
+    assert torch.equal(gs13[valid], s13[valid]) and torch.equal(gr13[valid], r13[valid])
 
     # W13 + SwiGLU (rows by sorted position)
     inter = torch.zeros((cap, I), dtype=torch.bfloat16, device=DEV)
