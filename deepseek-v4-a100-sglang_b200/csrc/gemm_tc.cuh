@@ -151,8 +151,14 @@ struct TcGemmCfg {
   // A ring (decoded weights in TMEM, 64 columns = 256 K per slot) and B ring
   // (token tiles in shared memory) have their own depths and barriers
   // (192-token tiles: a 2-slot A ring leaves TMEM room for two accumulators,
-  // so the next item's MMAs overlap the epilogue; the decode runs far ahead)
-  static constexpr int kStagesA = TN <= 64 ? 6 : (TN == 192 ? 2 : 4);
+  // so the next item's MMAs overlap the epilogue; 256-token tiles: a 2-slot
+  // A ring leaves room for the epilogue's bf16 stash)
+  static constexpr int kStagesA = TN <= 64 ? 6 : (TN >= 192 ? 2 : 4);
+  // 256-token tiles (one accumulator of 256 columns): the epilogue first
+  // converts the whole accumulator to bf16 pairs in a 128-column TMEM stash
+  // and hands the accumulator back, then transposes and stores from the
+  // stash while the next item's MMAs run
+  static constexpr int kStashCols = TN == 256 ? 128 : 0;
   static constexpr int kStagesB = TN <= 64 ? 6 : (TN <= 128 ? 4 : 2);
   // One barrier pair per stage for both operands: the token-tile loader
   // arrives (with its bytes) on the A slot's ready barrier, and reuses B slot
@@ -163,9 +169,11 @@ struct TcGemmCfg {
   // phase (stage g - kStagesA) has completed before the loader arrives.
   // accumulator sets per issuer: two where TMEM has room, so the MMAs of the
   // next item do not wait for the epilogue of this one
-  static constexpr int kAccSlots = kIssuers * 2 * kAccCols + kStagesA * 64 <= 512 ? 2 : 1;
-  // TMEM (512 columns): [issuer accumulators], then 64-column A slots
-  static constexpr int kAColBase = kIssuers * kAccSlots * kAccCols;
+  static constexpr int kAccSlots =
+      kIssuers * 2 * kAccCols + kStagesA * 64 + kStashCols <= 512 ? 2 : 1;
+  // TMEM (512 columns): [issuer accumulators], [stash], then 64-column A slots
+  static constexpr int kStashBase = kIssuers * kAccSlots * kAccCols;
+  static constexpr int kAColBase = kStashBase + kStashCols;
   static constexpr int kTmemCols = 512;
   // epilogue staging, per epilogue group: 16 token columns x 128 rows bf16
   static constexpr int kStgBytes = (kEpiWarps / 4) * 16 * 128 * 2;
@@ -695,19 +703,15 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         }
       };
 
-      if (EPI == kEpiSwiglu) {
-        // lanes 0..15: gate of channels j0 + 16*quarter + (lane & 15); lanes
-        // 16..31: up of the same channels.  Gate lanes finish tokens 0..7,
-        // up lanes tokens 8..15, after swapping the other half by shuffle.
-        const int j0 = it.y * 64;
-        const bool is_gate = lane < 16;
-        const int chl = lane & 15;
-        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
-          int32_t v[16];
-          load16(c0, v);
-          uint32_t pk[8];
-          scale16(c0, v, pk);
-          // own bf16 pairs: tokens (2p, 2p+1) in pk[p]
+      // the chunk's output from its 16 scaled bf16 values (pk[p]: tokens 2p, 2p+1)
+      auto emit16 = [&](int c0, const uint32_t (&pk)[8]) {
+        if constexpr (EPI == kEpiSwiglu) {
+          // lanes 0..15: gate of channels j0 + 16*quarter + (lane & 15); lanes
+          // 16..31: up of the same channels.  Gate lanes finish tokens 0..7,
+          // up lanes tokens 8..15, after swapping the other half by shuffle.
+          const int j0 = it.y * 64;
+          const bool is_gate = lane < 16;
+          const int chl = lane & 15;
           uint32_t mine[4], other[4];
 #pragma unroll
           for (int pp = 0; pp < 4; ++pp) {
@@ -777,60 +781,90 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
                                         16 * quarter + 8 * half) = hq;
           }
           __syncwarp();
+        } else {
+          // transpose through the warp's staging slice [16 tokens][32
+          // channels]: lane 8a + i then stores channels 8a..8a+7 of tokens
+          // i and 8 + i as two 16-byte stores (each token row of the warp
+          // is 64 contiguous bytes).  32-bit words of two neighbouring
+          // channels: lane pairs (2j, 2j+1) swap halves by shuffle, the even
+          // lane then writes tokens 0..7 and the odd lane tokens 8..15 of
+          // channels (2j, 2j+1); rows of opposite parity in one store keep
+          // the two lane sets on different banks
+          {
+            const uint32_t odd = lane & 1;
+            const int tb = odd ? 8 : 0, j = lane >> 1;
+            uint32_t* s32 = reinterpret_cast<uint32_t*>(stw);
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const uint32_t par = __shfl_xor_sync(0xffffffffu, odd ? pk[qq] : pk[4 + qq], 1);
+              const uint32_t own = odd ? pk[4 + qq] : pk[qq];
+              const uint32_t ev = odd ? par : own, od = odd ? own : par;
+              const uint32_t w0 = (ev & 0xFFFFu) | (od << 16);          // token tb + 2qq
+              const uint32_t w1 = (ev >> 16) | (od & 0xFFFF0000u);      // token tb + 2qq + 1
+              s32[(tb + 2 * qq + odd) * 16 + j] = odd ? w1 : w0;
+              s32[(tb + 2 * qq + 1 - odd) * 16 + j] = odd ? w0 : w1;
+            }
+          }
+          __syncwarp();
+          const int i = lane & 7, a8 = (lane >> 3) * 8;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int tok = 8 * h + i;
+            const int orow = orow_s[c0 + tok];
+            const uint4 val = *reinterpret_cast<const uint4*>(stw + tok * 32 + a8);
+            if (orow >= 0)
+              *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo +
+                                        it.y * 128 + quarter * 32 + a8) = val;
+          }
+          __syncwarp();
         }
-      } else {
+      };
+
+      if constexpr (EPI == kEpiI32) {
         const int n_g = it.y * 128 + row_local;
         for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
           int32_t v[16];
           load16(c0, v);
-          if (EPI == kEpiBf16) {
-            // transpose through the warp's staging slice [16 tokens][32
-            // channels]: lane 8a + i then stores channels 8a..8a+7 of tokens
-            // i and 8 + i as two 16-byte stores (each token row of the warp
-            // is 64 contiguous bytes)
-            uint32_t pk[8];
-            scale16(c0, v, pk);
-            // 32-bit words of two neighbouring channels: lane pairs (2j, 2j+1)
-            // swap halves by shuffle, the even lane then writes tokens 0..7
-            // and the odd lane tokens 8..15 of channels (2j, 2j+1); rows of
-            // opposite parity in one store keep the two lane sets on
-            // different banks (2-byte stores put two lanes on one word)
-            {
-              const uint32_t odd = lane & 1;
-              const int tb = odd ? 8 : 0, j = lane >> 1;
-              uint32_t* s32 = reinterpret_cast<uint32_t*>(stw);
 #pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                const uint32_t par = __shfl_xor_sync(0xffffffffu, odd ? pk[qq] : pk[4 + qq], 1);
-                const uint32_t own = odd ? pk[4 + qq] : pk[qq];
-                const uint32_t ev = odd ? par : own, od = odd ? own : par;
-                const uint32_t w0 = (ev & 0xFFFFu) | (od << 16);          // token tb + 2qq
-                const uint32_t w1 = (ev >> 16) | (od & 0xFFFF0000u);      // token tb + 2qq + 1
-                s32[(tb + 2 * qq + odd) * 16 + j] = odd ? w1 : w0;
-                s32[(tb + 2 * qq + 1 - odd) * 16 + j] = odd ? w0 : w1;
-              }
-            }
-            __syncwarp();
-            const int i = lane & 7, a8 = (lane >> 3) * 8;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int tok = 8 * h + i;
-              const int orow = orow_s[c0 + tok];
-              const uint4 val = *reinterpret_cast<const uint4*>(stw + tok * 32 + a8);
-              if (orow >= 0)
-                *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(orow) * p.ldo +
-                                          it.y * 128 + quarter * 32 + a8) = val;
-            }
-            __syncwarp();
-          } else {
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const int orow = orow_s[c0 + q];
-              if (orow < 0) continue;
-              p.out_i32[static_cast<int64_t>(it.z) * p.split_stride +
-                        static_cast<int64_t>(orow) * p.ldo + n_g] = v[q];
-            }
+          for (int q = 0; q < 16; ++q) {
+            const int orow = orow_s[c0 + q];
+            if (orow < 0) continue;
+            p.out_i32[static_cast<int64_t>(it.z) * p.split_stride +
+                      static_cast<int64_t>(orow) * p.ldo + n_g] = v[q];
           }
+        }
+      } else if constexpr (C::kStashCols > 0) {
+        // phase 1: the whole accumulator -> scaled bf16 pairs in the stash
+        // (8 columns per 16-token chunk); the accumulator is handed back
+        // after the last chunk's load, so the next item's MMAs start now
+        const uint32_t st0 = tmem + C::kStashBase + (static_cast<uint32_t>(quarter * 32) << 16);
+        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
+          int32_t v[16];
+          load16(c0, v);
+          uint32_t pk[8];
+          scale16(c0, v, pk);
+          tmem_st_x8(st0 + c0 / 2, pk);
+        }
+        tmem_st_wait();
+        // phase 2: transpose and store from the stash, the next chunk's
+        // stash load in flight during this chunk's work
+        uint32_t nx[8];
+        if (16 * eh < n_mma) tmem_ld_x8(st0 + 8 * eh, nx);
+        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
+          tmem_ld_wait_regs8(nx);
+          uint32_t pk[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) pk[q] = nx[q];
+          if (c0 + 16 * EH < n_mma) tmem_ld_x8(st0 + (c0 + 16 * EH) / 2, nx);
+          emit16(c0, pk);
+        }
+      } else {
+        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
+          int32_t v[16];
+          load16(c0, v);
+          uint32_t pk[8];
+          scale16(c0, v, pk);
+          emit16(c0, pk);
         }
       }
       if (!acc_released) {  // a group with no chunk of this item

@@ -20,6 +20,7 @@ from .mxfp4_int8_moe import (  # noqa: F401
     router_topk,
     router_align,
     mxfp4_int8_moe_forward_from_logits,
+    Mxfp4Int8MoeGraph,
 )
 from .jit_ops import (  # noqa: F401
     mxfp4_int8_dense_gemm,

@@ -520,3 +520,63 @@ def mxfp4_int8_moe_forward_quantized(a_q: torch.Tensor, a_scale: torch.Tensor,
                      intermediate_size=intermediate_size,
                      routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit,
                      masked=True)
+
+
+class Mxfp4Int8MoeGraph:
+    """:func:`mxfp4_int8_moe_forward` for a fixed token count, captured once
+    into a CUDA graph and replayed: the serving form of the decode layer (the
+    reference runs under SGLang's CUDA-graph decode, where the layer's host
+    work is paid at capture, not per step).  The launches, kernels and
+    results are those of :func:`mxfp4_int8_moe_forward`, bit for bit.
+
+    Inputs live in static device buffers (``hidden_states``, ``topk_ids``,
+    ``topk_weights``): write them, or pass tensors to :meth:`__call__`, which
+    copies them in on the current stream.  The output is the static tensor
+    ``out``, overwritten by the next replay."""
+
+    def __init__(self, weights: Mxfp4Int8MoeWeights, num_tokens: int, topk: int, *,
+                 hidden_size: int, intermediate_size: int,
+                 routed_scaling_factor: float | None = None,
+                 clamp_limit: float | None = None, device=None):
+        if num_tokens < 1:
+            raise ValueError("num_tokens must be positive")
+        dev = torch.device(device) if device is not None else weights.w13_mxfp4.device
+        _require_cuda(weights.w13_mxfp4, "weights")
+        self.num_tokens, self.topk = num_tokens, topk
+        self.hidden_states = torch.zeros((num_tokens, hidden_size), dtype=torch.bfloat16,
+                                         device=dev)
+        # any valid routing for the capture (the graph holds no routing)
+        experts = weights.w13_mxfp4.shape[0]
+        self.topk_ids = (torch.arange(num_tokens * topk, device=dev, dtype=torch.int32)
+                         % experts).view(num_tokens, topk)
+        self.topk_weights = torch.full((num_tokens, topk), 1.0 / topk, dtype=torch.float32,
+                                       device=dev)
+        kw = dict(hidden_size=hidden_size, intermediate_size=intermediate_size,
+                  routed_scaling_factor=routed_scaling_factor, clamp_limit=clamp_limit)
+
+        def fwd():
+            return mxfp4_int8_moe_forward(self.hidden_states, weights, self.topk_ids,
+                                          self.topk_weights, **kw)
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # loads the library, warms the allocator
+                fwd()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = fwd()
+
+    def __call__(self, hidden_states: torch.Tensor | None = None,
+                 topk_ids: torch.Tensor | None = None,
+                 topk_weights: torch.Tensor | None = None) -> torch.Tensor:
+        if hidden_states is not None:
+            self.hidden_states.copy_(hidden_states, non_blocking=True)
+        if topk_ids is not None:
+            self.topk_ids.copy_(topk_ids, non_blocking=True)
+        if topk_weights is not None:
+            self.topk_weights.copy_(topk_weights, non_blocking=True)
+        self.graph.replay()
+        return self.out
