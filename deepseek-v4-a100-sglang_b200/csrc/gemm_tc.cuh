@@ -201,7 +201,11 @@ struct TcGemmCfg {
   static constexpr int kDecodeWarps = 4 * kDecodeGroups;
   static constexpr int kDecBase = 4 + kEpiWarps;
   static constexpr int kIssuer1Warp = kDecBase + kDecodeWarps;
-  static constexpr int kWarps = kIssuer1Warp + kIssuers - 1;
+  // idle warps so that issuers 1.. start on sub-partition 2 (issuer 0 is
+  // warp 1, sub-partition 1): no sub-partition carries two issuers beside its
+  // three ALU-bound decode warps (decode W2 -2 %)
+  static constexpr int kIssuerPad = kIssuers > 1 ? (2 - kIssuer1Warp % 4 + 4) % 4 : 0;
+  static constexpr int kWarps = kIssuer1Warp + kIssuerPad + kIssuers - 1;
   static constexpr int kThreads = kWarps * 32;
   static_assert(TN % 16 == 0 && TN >= 16 && TN <= 256, "token tile");
   static_assert(kStagesA % kDecodeGroups == 0 && kStagesA % kIssuers == 0 &&
@@ -229,7 +233,9 @@ struct Item {
   bool valid;
 };
 
-__device__ __forceinline__ Item get_item(const TcGemmParams& p, int i, int n_blocks) {
+// Item i of the persistent walk; `expert` is the expert id of its block
+// (MoE), read ahead by ItemWalk.
+__device__ __forceinline__ Item make_item(const TcGemmParams& p, int i, int expert) {
   Item it;
   if (p.moe) {
     // row tile fastest: CTAs running side by side stream neighbouring 2 KB
@@ -237,7 +243,7 @@ __device__ __forceinline__ Item get_item(const TcGemmParams& p, int i, int n_blo
     it.z = 0;
     it.y = i % p.row_tiles;
     it.b = i / p.row_tiles;
-    it.expert = __ldg(p.expert_ids + it.b);
+    it.expert = expert;
     it.valid = it.expert >= 0;
   } else {
     it.z = i % p.splits;
@@ -249,6 +255,45 @@ __device__ __forceinline__ Item get_item(const TcGemmParams& p, int i, int n_blo
   }
   return it;
 }
+
+// Every role walks items blockIdx.x, blockIdx.x + gridDim.x, ...  For MoE
+// items the walk keeps (row tile, block) up to date by addition (no integer
+// division by the run-time row-tile count at each item start: that chain of
+// dependent instructions cost ~1,000 cycles of a decode warp per item) and
+// reads the next item's expert id while the current item runs.
+struct ItemWalk {
+  const TcGemmParams& p;
+  int n_items;
+  int y, b, dy, db;  // MoE: coordinates of the next item; step per gridDim.x
+  int e_next;
+  __device__ __forceinline__ ItemWalk(const TcGemmParams& p_, int n) : p(p_), n_items(n) {
+    const int i0 = blockIdx.x, G = gridDim.x;
+    y = i0 % p.row_tiles;
+    b = i0 / p.row_tiles;
+    dy = G % p.row_tiles;
+    db = G / p.row_tiles;
+    e_next = (p.moe && i0 < n_items) ? __ldg(p.expert_ids + b) : 0;
+  }
+  // item i (the walk's current one, i = blockIdx.x + k gridDim.x in order);
+  // starts the read of the next
+  __device__ __forceinline__ Item get(int i) {
+    if (!p.moe) return make_item(p, i, 0);
+    Item it;
+    it.z = 0;
+    it.y = y;
+    it.b = b;
+    it.expert = e_next;
+    it.valid = it.expert >= 0;
+    y += dy;
+    b += db;
+    if (y >= p.row_tiles) {
+      y -= p.row_tiles;
+      ++b;
+    }
+    e_next = (i + static_cast<int>(gridDim.x) < n_items) ? __ldg(p.expert_ids + b) : 0;
+    return it;
+  }
+};
 
 template <int TN, int EPIF>
 __global__ void __launch_bounds__(TcGemmCfg<TN>::kThreads, 1)
@@ -357,8 +402,9 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const uint64_t pol = l2_policy_evict_first();
       const uint32_t sh_bytes = static_cast<uint32_t>(p.sh_rows) * 128u;
       uint32_t g = 0, cc = 0;
+      ItemWalk walk(p, n_items);
       for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-        const Item it = get_item(p, i, n_blocks);
+        const Item it = walk.get(i);
         if (!it.valid) continue;
         int ks0, nks;
         k_range(it, ks0, nks);
@@ -395,14 +441,16 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         }
       }
     }
-  } else if (warp == 1 || warp >= C::kIssuer1Warp) {
+  } else if (warp == 1 || warp >= C::kIssuer1Warp + C::kIssuerPad) {
     // ------------------------------- MMA issuers -------------------------------
-    const int j = warp == 1 ? 0 : warp - C::kIssuer1Warp + 1;  // takes stages g = j (mod kIssuers)
+    // takes stages g = j (mod kIssuers)
+    const int j = warp == 1 ? 0 : warp - C::kIssuer1Warp - C::kIssuerPad + 1;
     if (lane == 0 && j < C::kIssuers) {
       uint32_t g = 0, t = 0;
       const uint64_t bdesc0 = smem_desc_sw128(smem_u32(smem + C::kOffB));
+      ItemWalk walk(p, n_items);
       for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-        const Item it = get_item(p, i, n_blocks);
+        const Item it = walk.get(i);
         if (!it.valid) continue;
         int ks0, nks;
         k_range(it, ks0, nks);
@@ -453,8 +501,9 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       if (lane == 0) {
         tma_prefetch_desc(&p.map_act);
         uint32_t g = 0;
+        ItemWalk walk(p, n_items);
         for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-          const Item it = get_item(p, i, n_blocks);
+          const Item it = walk.get(i);
           if (!it.valid) continue;
           int ks0, nks;
           k_range(it, ks0, nks);
@@ -487,8 +536,9 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const int gt = tid - 64;  // < nthr
       uint32_t g = 0, t = 0;
       if (gt == 0 && !tiled) tma_prefetch_desc(&p.map_act);
+      ItemWalk walk(p, n_items);
       for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-        const Item it = get_item(p, i, n_blocks);
+        const Item it = walk.get(i);
         if (!it.valid) continue;
         int ks0, nks;
         k_range(it, ks0, nks);
@@ -620,8 +670,9 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     uint16_t* stw = reinterpret_cast<uint16_t*>(smem + C::kOffStg + (warp - 4) * 1024);
     const float lim = p.has_clamp ? __bfloat162float(f2bf(p.clamp_limit)) : 0.f;
     uint32_t t = 0, g = 0;
+    ItemWalk walk(p, n_items);
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-      const Item it = get_item(p, i, n_blocks);
+      const Item it = walk.get(i);
       if (!it.valid) continue;
       int ks0, nks;
       k_range(it, ks0, nks);
@@ -889,8 +940,9 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16, one = p.dec_one;
     uint32_t g = 0, cc = 0;
+    ItemWalk walk(p, n_items);
     for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
-      const Item it = get_item(p, i, n_blocks);
+      const Item it = walk.get(i);
       if (!it.valid) continue;
       int ks0, nks;
       k_range(it, ks0, nks);
@@ -917,6 +969,11 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           uint32_t shw[2];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) shw[hh] = SH[hh * 128 + row];
+          // decode of 8 weights (biased unsigned on the sorted path)
+          auto dec8 = [&](uint32_t q, uint32_t a0, uint32_t a1, uint32_t& lo, uint32_t& hi) {
+            if (kBiased) decode8_u8(q, a0, a1, one, m1, hi16, lo, hi);
+            else decode8_fma(q, a0, a1, m1, hi16, lo, hi);
+          };
           // all 8 packed units first (a 128-K tail stage decodes stale bytes
           // into columns the MMA never reads)
           uint4 wv[8];
@@ -940,23 +997,12 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
               uint32_t a0, a1;
               decode_tables((shw[kb >> 2] >> (2 * (kb & 3))) & 3u, a0, a1);
               // columns 8*kbi + 0..3: k 0..15 of the block, 8*kbi + 4..7: k 16..31
-              if (kBiased) {
-                decode8_u8(w.x, a0, a1, one, m1, hi16, v[8 * kbi + 0], v[8 * kbi + 4]);
-                decode8_u8(w.y, a0, a1, one, m1, hi16, v[8 * kbi + 1], v[8 * kbi + 5]);
-                decode8_u8(w.z, a0, a1, one, m1, hi16, v[8 * kbi + 2], v[8 * kbi + 6]);
-                decode8_u8(w.w, a0, a1, one, m1, hi16, v[8 * kbi + 3], v[8 * kbi + 7]);
-              } else {
-                decode8_fma(w.x, a0, a1, m1, hi16, v[8 * kbi + 0], v[8 * kbi + 4]);
-                decode8_fma(w.y, a0, a1, m1, hi16, v[8 * kbi + 1], v[8 * kbi + 5]);
-                decode8_fma(w.z, a0, a1, m1, hi16, v[8 * kbi + 2], v[8 * kbi + 6]);
-                decode8_fma(w.w, a0, a1, m1, hi16, v[8 * kbi + 3], v[8 * kbi + 7]);
-              }
+              dec8(w.x, a0, a1, v[8 * kbi + 0], v[8 * kbi + 4]);
+              dec8(w.y, a0, a1, v[8 * kbi + 1], v[8 * kbi + 5]);
+              dec8(w.z, a0, a1, v[8 * kbi + 2], v[8 * kbi + 6]);
+              dec8(w.w, a0, a1, v[8 * kbi + 3], v[8 * kbi + 7]);
             }
-#ifdef DSV4_TRACE_NOST
-            if (v[0] == 0x12345678u && v[5] == 0x9abcdef0u) tmem_st_x16(tcol + 16 * q, v);
-#else
             tmem_st_x16(tcol + 16 * q, v);
-#endif
           }
           // The packed slot goes back to the TMA producer only after the
           // decode has consumed the loaded registers.  Handing it back right
