@@ -70,6 +70,38 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
   (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Cluster-of-2 launch (CTA pairs of the 2-SM MMA), with programmatic
+// dependent launch as launch_pdl.
+template <typename... KArgs, typename... Args>
+void launch_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                 Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// 256-token tiles run on CTA pairs only with DSV4_B200_PAIR=1 (read at each
+// launch, so one process can compare both forms).  Off by default: measured
+// slower than single CTAs (prefill 4.06 vs 3.32 ms) — the cross-SM hand-off
+// of every stage (remote cluster-scope arrivals) is not hidden by the 2-slot
+// A ring that the TMEM stash leaves.
+bool pair_enabled() {
+  const char* e = std::getenv("DSV4_B200_PAIR");
+  return e != nullptr && std::strcmp(e, "1") == 0;
+}
+
 constexpr int kMaxDevices = 64;
 std::mutex g_init_mu;
 bool g_inited[kMaxDevices] = {};
@@ -77,7 +109,7 @@ int g_sm_count[kMaxDevices] = {};
 
 template <int TN, int EPI>
 struct GemmKernel {
-  static constexpr int kSmem = TcGemmCfg<TN>::kSmemLaunch;
+  static constexpr int kSmem = TcGemmCfg<TN, (EPI & kEpiPair) != 0>::kSmemLaunch;
   static void* fn() { return reinterpret_cast<void*>(&mxfp4_int8_tc_gemm_kernel<TN, EPI>); }
 };
 
@@ -120,6 +152,15 @@ int ensure_init() {
   if (e == cudaSuccess) e = set_attrs_epi<kEpiSwiglu>();
   if (e == cudaSuccess) e = set_attrs_epi<kEpiBf16 | kEpiBiased>();
   if (e == cudaSuccess) e = set_attrs_epi<kEpiSwiglu | kEpiBiased>();
+  // CTA-pair instantiations exist for 256-token tiles only
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(GemmKernel<256, kEpiBf16 | kEpiBiased | kEpiPair>::fn(),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GemmKernel<256, kEpiBf16 | kEpiBiased | kEpiPair>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(GemmKernel<256, kEpiSwiglu | kEpiBiased | kEpiPair>::fn(),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GemmKernel<256, kEpiSwiglu | kEpiBiased | kEpiPair>::kSmem);
   if (e == cudaSuccess) e = set_router_align_attrs();
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(reinterpret_cast<void*>(&moe_align_kernel),
@@ -136,6 +177,20 @@ int sm_count() {
   int dev = 0;
   cudaGetDevice(&dev);
   return g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
+}
+
+// Persistent launch of CTA pairs: one pair per two SMs, never more pairs than
+// pair items (an item = one token tile x two neighbouring row tiles).
+template <int EPI>
+int launch_gemm_pair(int64_t max_pair_items, const TcGemmParams& p, cudaStream_t st) {
+  int64_t pairs = sm_count() / 2;
+  if (max_pair_items < pairs) pairs = max_pair_items;
+  if (pairs <= 0) return DSV4_OK;
+  const dim3 grid(static_cast<unsigned>(2 * pairs));
+  constexpr int kE = EPI | kEpiPair;
+  launch_pair(&mxfp4_int8_tc_gemm_kernel<256, kE>, grid, TcGemmCfg<256, true>::kThreads,
+              GemmKernel<256, kE>::kSmem, st, p);
+  return check_launch("mxfp4_int8_tc_gemm_kernel (CTA pairs)");
 }
 
 // Persistent launch: one CTA per SM (never more CTAs than work items).
@@ -251,7 +306,8 @@ int shift_chunk_rows(int stages_per_item, int tn) {
 //   b_mode 1: int8 [rows][k] as 2-D {k, rows}, box {128, tn}
 //   b_mode 2: int8 K-chunk-major [k/128][rows][128] as 3-D {128, rows, k/128},
 //             box {128, tn, 2} (both 128-K halves of a stage in one copy)
-int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, int b_mode, int tn) {
+int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, int b_mode, int tn,
+                   bool pair = false) {
   DSV4_REQUIRE(tn <= 128 || b_mode == 2, "192/256-token tiles need K-chunk-major token rows");
   if (tensor_map_encoder() == nullptr) return fail(DSV4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   DSV4_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, "a_q must be 16-byte aligned");
@@ -261,7 +317,8 @@ int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, in
     DSV4_REQUIRE(k % 128 == 0, "K-chunk-major rows need K %% 128 == 0");
     cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(k / 128)};
     cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(rows) * 128};
-    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(tn), 2};
+    // CTA pairs: each CTA stages half of the token tile
+    cuuint32_t box[3] = {128, static_cast<cuuint32_t>(pair ? tn / 2 : tn), 2};
     r = encode_u8(&p.map_act, 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   } else {
@@ -361,10 +418,19 @@ int moe_gemm_common(int epi, const int8_t* a_q, const float* a_scale, int64_t m_
   if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, experts, k / 32, shift_stride, n_rows / 8,
                                  epi == kEpiSwiglu, inter, shift_chunk_rows(p.k_stages, static_cast<int>(block_m))))
     return r;
-  if (int r = encode_act_map(p, a_q, m_in, k, sorted_rows ? 2 : 0, static_cast<int>(block_m)))
+  // 256-token tiles of the sorted path: CTA pairs (each CTA its own row tile
+  // of a neighbouring pair, half of the token tile)
+  const bool pair = pair_enabled() && block_m == 256 && sorted_rows && a_rowsum != nullptr &&
+                    tile_rows_y % 2 == 0;
+  if (int r = encode_act_map(p, a_q, m_in, k, sorted_rows ? 2 : 0, static_cast<int>(block_m), pair))
     return r;
   const int64_t max_items = grid_m * tile_rows_y;
   const int bm = static_cast<int>(block_m);
+  if (pair) {
+    if (epi == kEpiSwiglu)
+      return launch_gemm_pair<kEpiSwiglu | kEpiBiased>(max_items / 2, p, as_stream(stream));
+    return launch_gemm_pair<kEpiBf16 | kEpiBiased>(max_items / 2, p, as_stream(stream));
+  }
   if (a_rowsum != nullptr) {  // biased-unsigned decode, corrected by the row sums
     if (epi == kEpiSwiglu)
       return launch_gemm<kEpiSwiglu | kEpiBiased>(bm, max_items, p, as_stream(stream));
@@ -419,10 +485,12 @@ int dense_common(const int8_t* a_q, const float* a_scale, int64_t m, int64_t k,
   if (int r = encode_weight_maps(p, b_mxfp4, b_shift2, 1, k / 32, shift_stride, n / 8, false, 0,
                                  shift_chunk_rows(p.stages_per_split, tn)))
     return r;
-  if (int r = encode_act_map(p, a_q, m, k, cm ? 2 : 1, tn)) return r;
+  const bool pair = cm && pair_enabled() && (n / 128) % 2 == 0;
+  if (int r = encode_act_map(p, a_q, m, k, cm ? 2 : 1, tn, pair)) return r;
   p.m_tiles = static_cast<int>((m + tn - 1) / tn);
   p.row_tiles = static_cast<int>(n / 128);
   const int64_t max_items = static_cast<int64_t>(p.m_tiles) * p.row_tiles * p.splits;
+  if (pair) return launch_gemm_pair<kEpiBf16 | kEpiBiased>(max_items / 2, p, as_stream(stream));
   if (cm) return launch_gemm<kEpiBf16 | kEpiBiased>(tn, max_items, p, as_stream(stream));
   if (epi == kEpiI32) return launch_gemm<kEpiI32>(tn, max_items, p, as_stream(stream));
   return launch_gemm<kEpiBf16>(tn, max_items, p, as_stream(stream));

@@ -58,6 +58,13 @@ enum Epilogue : int { kEpiBf16 = 0, kEpiI32 = 1, kEpiSwiglu = 2 };
 // every accumulator (needs per-row int8 sums over the item's K range, i.e.
 // MoE items, which cover all of K).
 constexpr int kEpiBiased = 4;
+// Flag or-ed into the kernel's epilogue parameter: 256-token tiles on a CTA
+// pair (cluster of 2, tcgen05.mma.cta_group::2, M = 256): each CTA decodes
+// its own 128 weight rows and stages half of the token tile (tokens
+// 128 r .. 128 r + 127 in CTA rank r), and the even CTA issues the MMAs for
+// both.  Per SM a stage copies 48.5 KB instead of 80.5 KB.  Selected only
+// with DSV4_B200_PAIR=1 (measured slower than single CTAs).
+constexpr int kEpiPair = 8;
 
 struct TcGemmParams {
   // Weight tensor maps (uint8):
@@ -124,10 +131,12 @@ struct TcGemmParams {
 //   gather warp   g % 2               -> 2 | kStagesB
 //   token loader  waits for stage g - kStagesB on its A-slot empty barrier
 //                 (safe while kStagesA >= kStagesB, see TcGemmCfg)
-template <int TN>
+template <int TN, bool PAIR = false>
 struct TcGemmCfg {
-  static constexpr int kBHalf = TN * 128;        // one 128-K SW128 sub-tile of B
-  static constexpr int kBBytes = 2 * kBHalf;     // TN token rows x 256 K (int8)
+  static_assert(!PAIR || TN == 256, "CTA pairs run 256-token tiles");
+  static constexpr int kBRows = PAIR ? TN / 2 : TN;  // token rows staged by this CTA
+  static constexpr int kBHalf = kBRows * 128;    // one 128-K SW128 sub-tile of B
+  static constexpr int kBBytes = 2 * kBHalf;     // kBRows token rows x 256 K (int8)
   static constexpr int kPBytes = 128 * 256 / 2;  // packed FP4 codes of one 256-K stage
   // shift chunks: the 2-bit shifts of kShChunk stages, [2 * kShChunk rows][128 B]
   // (row = one 4-block shift word per output row; SwiGLU: gate 64 B | up 64 B)
@@ -256,41 +265,50 @@ __device__ __forceinline__ Item make_item(const TcGemmParams& p, int i, int expe
   return it;
 }
 
-// Every role walks items blockIdx.x, blockIdx.x + gridDim.x, ...  For MoE
+// Every role walks items i0, i0 + G, ... (i0 = blockIdx.x, G = gridDim.x;
+// CTA pairs: i0 = cluster index, G = number of clusters, and an item covers
+// two neighbouring row tiles, CTA rank r taking row tile 2 y + r).  For MoE
 // items the walk keeps (row tile, block) up to date by addition (no integer
 // division by the run-time row-tile count at each item start: that chain of
 // dependent instructions cost ~1,000 cycles of a decode warp per item) and
 // reads the next item's expert id while the current item runs.
 struct ItemWalk {
   const TcGemmParams& p;
-  int n_items;
-  int y, b, dy, db;  // MoE: coordinates of the next item; step per gridDim.x
+  int n_items, G, rt, rank;  // rank: CTA rank in the pair, -1 without pairs
+  int y, b, dy, db;          // MoE: coordinates of the next item; step per G
   int e_next;
-  __device__ __forceinline__ ItemWalk(const TcGemmParams& p_, int n) : p(p_), n_items(n) {
-    const int i0 = blockIdx.x, G = gridDim.x;
-    y = i0 % p.row_tiles;
-    b = i0 / p.row_tiles;
-    dy = G % p.row_tiles;
-    db = G / p.row_tiles;
+  __device__ __forceinline__ ItemWalk(const TcGemmParams& p_, int n, int i0, int G_, int rank_)
+      : p(p_), n_items(n), G(G_), rank(rank_) {
+    rt = rank >= 0 ? p.row_tiles / 2 : p.row_tiles;
+    y = i0 % rt;
+    b = i0 / rt;
+    dy = G % rt;
+    db = G / rt;
     e_next = (p.moe && i0 < n_items) ? __ldg(p.expert_ids + b) : 0;
   }
-  // item i (the walk's current one, i = blockIdx.x + k gridDim.x in order);
-  // starts the read of the next
+  // item i (the walk's current one, in order); starts the read of the next
   __device__ __forceinline__ Item get(int i) {
-    if (!p.moe) return make_item(p, i, 0);
     Item it;
+    if (!p.moe) {
+      it = make_item(p, i, 0);  // dense: pairs split row tiles as well
+      if (rank >= 0) {
+        const int r = i / p.splits;
+        it.y = 2 * (r / p.m_tiles) + rank;
+      }
+      return it;
+    }
     it.z = 0;
-    it.y = y;
+    it.y = rank >= 0 ? 2 * y + rank : y;
     it.b = b;
     it.expert = e_next;
     it.valid = it.expert >= 0;
     y += dy;
     b += db;
-    if (y >= p.row_tiles) {
-      y -= p.row_tiles;
+    if (y >= rt) {
+      y -= rt;
       ++b;
     }
-    e_next = (i + static_cast<int>(gridDim.x) < n_items) ? __ldg(p.expert_ids + b) : 0;
+    e_next = (i + G < n_items) ? __ldg(p.expert_ids + b) : 0;
     return it;
   }
 };
@@ -300,7 +318,8 @@ __global__ void __launch_bounds__(TcGemmCfg<TN>::kThreads, 1)
 mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   constexpr int EPI = EPIF & 3;
   constexpr bool kBiased = (EPIF & kEpiBiased) != 0;
-  using C = TcGemmCfg<TN>;
+  constexpr bool kPair = (EPIF & kEpiPair) != 0;
+  using C = TcGemmCfg<TN, kPair>;
   constexpr int SA = C::kStagesA;
   constexpr int SB = C::kStagesB;
   constexpr int SP = C::kStagesP;
@@ -311,16 +330,20 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   const int lane = tid & 31;
   pdl_entry();  // before the first global read (num_tokens_post_padded)
 
-  // ---- the item space (identical in every thread) ----
+  // ---- the item space (identical in every thread; CTA pairs: in both CTAs) ----
   int n_blocks, n_items;
+  const int row_items = kPair ? p.row_tiles / 2 : p.row_tiles;
   if (p.moe) {
     n_blocks = __ldg(p.ntpp) / p.block_m;
-    n_items = n_blocks * p.row_tiles;
+    n_items = n_blocks * row_items;
   } else {
     n_blocks = p.m_tiles;
-    n_items = p.m_tiles * p.row_tiles * p.splits;
+    n_items = p.m_tiles * row_items * p.splits;
   }
-  if (static_cast<int>(blockIdx.x) >= n_items) return;
+  const int i_first = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int i_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int pair_rank = kPair ? static_cast<int>(cluster_ctarank()) : -1;
+  if (i_first >= n_items) return;  // both CTAs of a pair leave together
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -354,13 +377,15 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       mbar_init(pk_full(s), 1);
       mbar_init(pk_empty(s), 4);
     }
+    // CTA pairs: the leader's a_full and acc_empty also count the peer's
+    // arrivals (its decode group and token-tile lane, its epilogue warps)
     for (int s = 0; s < SA; ++s) {
-      mbar_init(a_full(s), 4 + 1);  // one decode group (4 warps) + the token-tile lane
+      mbar_init(a_full(s), (kPair ? 2 : 1) * (4 + 1));  // decode group (4 warps) + token-tile lane
       mbar_init(a_empty(s), 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(acc_full(s), C::kIssuers);
-      mbar_init(acc_empty(s), C::kEpiWarps);
+      mbar_init(acc_empty(s), (kPair ? 2 : 1) * C::kEpiWarps);
     }
     for (int s = 0; s < SHS; ++s) {
       mbar_init(sh_full(s), 1);
@@ -374,13 +399,39 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     mbar_fence_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(s_tmem), C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(s_tmem), C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(s_tmem), C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // CTA pairs: both CTAs' barriers are initialised before any remote arrival
+  if constexpr (kPair) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  // barriers that pair traffic goes to: the leader's (rank 0) copy
+  auto leader = [&](uint32_t bar) { return kPair ? mapa_shared(bar, 0) : bar; };
+  // arrivals on the leader's barriers: CTA scope from the leader's own
+  // threads, cluster scope (remote) from the peer's
+  auto arrive_leader = [&](uint32_t bar) {
+    if (kPair && pair_rank != 0)
+      mbar_arrive_cl(leader(bar));
+    else
+      mbar_arrive(bar);
+  };
+  // waits on barriers the peer arrives on, or (in the peer) that the
+  // leader's pair commit signals, use cluster scope
+  auto wait_x = [&](uint32_t bar, uint32_t parity, int code) {
+    return kPair ? mbar_wait_cl(bar, parity, code) : mbar_wait(bar, parity, code);
+  };
+  auto wait_own = [&](uint32_t bar, uint32_t parity, int code) {
+    return (kPair && pair_rank != 0) ? mbar_wait_cl(bar, parity, code)
+                                     : mbar_wait(bar, parity, code);
+  };
 
   // stages are 256 K (8 blocks of 32); the last one of K may be 128 K
   auto k_range = [&](const Item& it, int& ks0, int& nks) {
@@ -402,8 +453,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const uint64_t pol = l2_policy_evict_first();
       const uint32_t sh_bytes = static_cast<uint32_t>(p.sh_rows) * 128u;
       uint32_t g = 0, cc = 0;
-      ItemWalk walk(p, n_items);
-      for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+      ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
+      for (int i = i_first; i < n_items; i += i_step) {
         const Item it = walk.get(i);
         if (!it.valid) continue;
         int ks0, nks;
@@ -445,11 +496,12 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     // ------------------------------- MMA issuers -------------------------------
     // takes stages g = j (mod kIssuers)
     const int j = warp == 1 ? 0 : warp - C::kIssuer1Warp - C::kIssuerPad + 1;
-    if (lane == 0 && j < C::kIssuers) {
+    // CTA pairs: the leader's issuer issues for both CTAs
+    if (lane == 0 && j < C::kIssuers && pair_rank <= 0) {
       uint32_t g = 0, t = 0;
       const uint64_t bdesc0 = smem_desc_sw128(smem_u32(smem + C::kOffB));
-      ItemWalk walk(p, n_items);
-      for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+      ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
+      for (int i = i_first; i < n_items; i += i_step) {
         const Item it = walk.get(i);
         if (!it.valid) continue;
         int ks0, nks;
@@ -457,8 +509,12 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         const int ms = t % MS;
         const int as = t % AS;
         mbar_wait(meta_full(ms), (t / MS) & 1, kErrWaitMeta);
-        const uint32_t idesc = kBiased ? idesc_u8s8(128, n_mma_of(ms)) : idesc_i8(128, n_mma_of(ms));
-        mbar_wait(acc_empty(as), ((t / AS) & 1) ^ 1, kErrWaitAccEmpty);
+        // CTA pairs: M = 256 (128 rows per CTA) and always N = 256, split
+        // 128 + 128 between the CTAs' token halves
+        const int n_cols = kPair ? TN : n_mma_of(ms);
+        const uint32_t m_rows = kPair ? 256u : 128u;
+        const uint32_t idesc = kBiased ? idesc_u8s8(m_rows, n_cols) : idesc_i8(m_rows, n_cols);
+        wait_x(acc_empty(as), ((t / AS) & 1) ^ 1, kErrWaitAccEmpty);
         if (j == 0) DSV4_TRACE_EV(12, t);
         tc_fence_after();
         const uint32_t d_tmem = tmem + (as * C::kIssuers + j) * C::kAccCols;
@@ -467,7 +523,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           const uint32_t gs = g + s;
           const int sa = gs % SA;
           DSV4_TRACE_EV(9, gs);
-          mbar_wait(a_full(sa), (gs / SA) & 1, kErrWaitAbFull);
+          wait_x(a_full(sa), (gs / SA) & 1, kErrWaitAbFull);
           DSV4_TRACE_EV(3, gs);
           const uint32_t a_tmem = tmem + C::kAColBase + sa * 64;
           tc_fence_after();
@@ -475,15 +531,31 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           const uint64_t bdesc = bdesc0 + static_cast<uint64_t>(((gs % SB) * C::kBBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            if (kk < nkb)
-              mma_i8_ts(d_tmem, a_tmem + kk * 8,
-                        bdesc + static_cast<uint64_t>(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4),
-                        idesc, (s > s_first || kk > 0) ? 1u : 0u);
+            if (kk < nkb) {
+              const uint64_t bd =
+                  bdesc + static_cast<uint64_t>(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4);
+              const uint32_t acc = (s > s_first || kk > 0) ? 1u : 0u;
+              if constexpr (kPair)
+                mma_i8_ts_pair(d_tmem, a_tmem + kk * 8, bd, idesc, acc);
+              else
+                mma_i8_ts(d_tmem, a_tmem + kk * 8, bd, idesc, acc);
+            }
           }
-          mma_commit(a_empty(sa));  // frees the A slot and (for the loader) the B slot
+          // frees the A slot and (for the loader) the B slot; pairs: in both CTAs
+          if constexpr (kPair) {
+            mma_commit_pair(mapa_shared(a_empty(sa), 0));
+            mma_commit_pair(mapa_shared(a_empty(sa), 1));
+          } else {
+            mma_commit(a_empty(sa));
+          }
           DSV4_TRACE_EV(6, gs);
         }
-        mma_commit(acc_full(as));
+        if constexpr (kPair) {
+          mma_commit_pair(mapa_shared(acc_full(as), 0));
+          mma_commit_pair(mapa_shared(acc_full(as), 1));
+        } else {
+          mma_commit(acc_full(as));
+        }
         g += nks;
         ++t;
       }
@@ -501,8 +573,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       if (lane == 0) {
         tma_prefetch_desc(&p.map_act);
         uint32_t g = 0;
-        ItemWalk walk(p, n_items);
-        for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+        ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
+        for (int i = i_first; i < n_items; i += i_step) {
           const Item it = walk.get(i);
           if (!it.valid) continue;
           int ks0, nks;
@@ -512,10 +584,19 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             const int sb = g % SB;
             const uint32_t ready = a_full(g % SA);
             if (g >= static_cast<uint32_t>(SB))  // B slot free once stage g - SB is done
-              mbar_wait(a_empty((g - SB) % SA), ((g - SB) / SA) & 1, kErrWaitAbEmpty);
+              wait_own(a_empty((g - SB) % SA), ((g - SB) / SA) & 1, kErrWaitAbEmpty);
             DSV4_TRACE_EV(7, g);
             const uint32_t b_base = smem_u32(smem + C::kOffB + sb * C::kBBytes);
-            if (p.b_mode == 2) {
+            if (kPair) {
+              // this CTA's half of the token tile, completing on the leader's barrier
+              const uint32_t rdy = leader(ready);
+              if (pair_rank != 0)
+                mbar_arrive_expect_tx_cl(rdy, static_cast<uint32_t>(C::kBBytes));
+              else
+                mbar_arrive_expect_tx(ready, static_cast<uint32_t>(C::kBBytes));
+              tma_load_3d_pair(b_base, &p.map_act, 0, row0 + pair_rank * C::kBRows,
+                               (ks0 + s) * 2, rdy, pol);
+            } else if (p.b_mode == 2) {
               // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves
               mbar_arrive_expect_tx(ready, static_cast<uint32_t>(C::kBBytes));
               tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ready, pol);
@@ -536,8 +617,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const int gt = tid - 64;  // < nthr
       uint32_t g = 0, t = 0;
       if (gt == 0 && !tiled) tma_prefetch_desc(&p.map_act);
-      ItemWalk walk(p, n_items);
-      for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+      ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
+      for (int i = i_first; i < n_items; i += i_step) {
         const Item it = walk.get(i);
         if (!it.valid) continue;
         int ks0, nks;
@@ -670,8 +751,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     uint16_t* stw = reinterpret_cast<uint16_t*>(smem + C::kOffStg + (warp - 4) * 1024);
     const float lim = p.has_clamp ? __bfloat162float(f2bf(p.clamp_limit)) : 0.f;
     uint32_t t = 0, g = 0;
-    ItemWalk walk(p, n_items);
-    for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+    ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
+    for (int i = i_first; i < n_items; i += i_step) {
       const Item it = walk.get(i);
       if (!it.valid) continue;
       int ks0, nks;
@@ -679,7 +760,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       const int ms = t % MS;
       const int as = t % AS;
       mbar_wait(meta_full(ms), (t / MS) & 1, kErrWaitMeta);
-      mbar_wait(acc_full(as), (t / AS) & 1, kErrWaitAccFull);
+      wait_own(acc_full(as), (t / AS) & 1, kErrWaitAccFull);
       if (tid == 128) DSV4_TRACE_EV(10, t);
       tc_fence_after();
       const int* orow_s = meta_orow(ms);
@@ -700,7 +781,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       auto release_acc = [&]() {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty(as));
+        if (lane == 0) arrive_leader(acc_empty(as));
         acc_released = true;
       };
       auto load16 = [&](int c0, int32_t (&v)[16]) {
@@ -940,8 +1021,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16, one = p.dec_one;
     uint32_t g = 0, cc = 0;
-    ItemWalk walk(p, n_items);
-    for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+    ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
+    for (int i = i_first; i < n_items; i += i_step) {
       const Item it = walk.get(i);
       if (!it.valid) continue;
       int ks0, nks;
@@ -983,7 +1064,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
             wv[kb] = *reinterpret_cast<const uint4*>(P + poff);
           }
           (void)nkb;
-          mbar_wait(a_empty(sa), ((gs / SA) & 1) ^ 1, kErrWaitAbEmpty);
+          wait_own(a_empty(sa), ((gs / SA) & 1) ^ 1, kErrWaitAbEmpty);
           if (lane == 0 && quarter == 0) DSV4_TRACE_EV(2, gs);
           tc_fence_after();
           const uint32_t tcol = tmem + t_lane + C::kAColBase + sa * 64;
@@ -1015,7 +1096,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(a_full(sa));
+          if (lane == 0) arrive_leader(a_full(sa));
           if (lane == 0 && quarter == 0) DSV4_TRACE_EV(5, gs);
         }
         __syncwarp();
@@ -1026,9 +1107,15 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   }
   tc_fence_before();
   __syncthreads();
+  // CTA pairs: neither CTA leaves while the other may still arrive on its
+  // barriers or read its shared memory
+  if constexpr (kPair) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem, C::kTmemCols);
+    else
+      tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 

@@ -248,3 +248,38 @@ def test_prefill_gemms_repeat_bit_identical(weights, kind):
                                      routed, s, e, n, **kw)
         assert torch.equal(routed[sl[valid]], ref_pos[valid])
     assert D.check_device_status() == 0
+
+
+@pytest.mark.parametrize("kind", ["zipf", "uniform"])
+def test_prefill_gemms_cta_pair_equals_single_cta(weights, kind, monkeypatch):
+    """The 256-token tiles on CTA pairs (cta_group::2, DSV4_B200_PAIR=1) and
+    on single CTAs (the default) give the same W13 and W2 outputs, bit for
+    bit, at the benchmarked prefill shape."""
+    raw, w = weights
+    m = 8192
+    ids, tw = _routing(m, 1500 if kind == "zipf" else 1600, kind)
+    x = G.randn_bf16((m, H), 1501).to(DEV)
+    nv = m * TOPK
+    bm = D.select_sorted_block_m(m, TOPK, E)
+    assert bm == 256
+    kw = dict(hidden_size=H, intermediate_size=I, topk=TOPK, block_m=bm, num_valid_tokens=nv)
+    s, e, n, spos = D.moe_align_block_size(ids.to(DEV), bm, E, return_slot_pos=True)
+    cap = s.numel()
+    a13, s13, r13 = J.quantize_scatter_int8(x, spos, cap, topk=TOPK, num_valid_tokens=nv)
+    outs = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("DSV4_B200_PAIR", mode)
+        inter = torch.zeros((cap, I), dtype=torch.bfloat16, device=DEV)
+        J.mxfp4_int8_moe_gemm_swiglu_sorted(a13, s13, r13, w.w13_mxfp4, w.w13_shift2,
+                                            w.w13_channel_scale, inter, s, e, n, **kw)
+        a2, s2, r2 = J.quantize_sorted_int8(inter, s, n, num_valid_tokens=nv)
+        routed = torch.zeros((nv, H), dtype=torch.bfloat16, device=DEV)
+        J.mxfp4_int8_moe_gemm_sorted(a2, s2, r2, w.w2_mxfp4, w.w2_shift2, w.w2_channel_scale,
+                                     routed, s, e, n, **kw)
+        torch.cuda.synchronize()
+        outs[mode] = (inter, routed)
+    sl = s.long()
+    valid = (torch.arange(cap, device=DEV) < int(n.item())) & (sl < nv)
+    assert torch.equal(outs["1"][0][valid], outs["0"][0][valid])
+    assert torch.equal(outs["1"][1], outs["0"][1])
+    assert D.check_device_status() == 0
