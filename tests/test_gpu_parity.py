@@ -73,6 +73,33 @@ def test_quant_ties_bit_exact(scale, dtype):
     np.testing.assert_array_equal(dq2.cpu().numpy(), q2)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_quant_reciprocal_path_bit_exact(dtype):
+    """The quantiser multiplies by fl(1/s) and divides only within 2^-12 of a
+    half-integer: values one to three ulp either side of (n + 0.5) s, for 64
+    unrelated row scales, against IEEE division (numpy float32)."""
+    rng = np.random.default_rng(5)
+    rows = []
+    for _ in range(64):
+        a = np.float32(rng.uniform(1e-3, 1e3))
+        sc = np.float32(a / np.float32(127.0))
+        n = rng.integers(-125, 125, size=256).astype(np.float32)
+        v = ((n + np.float32(0.5)) * sc).astype(np.float32)
+        k = rng.integers(-3, 4, size=256)
+        v = np.where(k > 0, np.nextafter(v, np.float32(np.inf)), v)
+        v = np.where(k < 0, np.nextafter(v, np.float32(-np.inf)), v)
+        v = np.where(np.abs(k) > 1, np.nextafter(v, np.float32(np.inf) * np.sign(k)), v)
+        v[0] = a
+        rows.append(v.astype(np.float32))
+    x = torch.from_numpy(np.stack(rows)).to(dtype)
+    q, qs = O.quantize_per_token_int8(x.float().numpy())
+    for xx in (x, torch.cat([x] * 16, dim=1)):  # K = 256 and 4096 row paths
+        dq, dqs = D.quantize_per_token_int8(xx.to(DEV))
+        oq, oqs = O.quantize_per_token_int8(xx.float().numpy())
+        np.testing.assert_array_equal(dq.cpu().numpy(), oq)
+        np.testing.assert_array_equal(dqs.cpu().numpy().view(np.uint32), oqs.view(np.uint32))
+
+
 @pytest.mark.parametrize("name", ["repack_span3", "repack_baseline", "repack_wide"])
 @pytest.mark.parametrize("variant", ["tri", "torch"])
 def test_repack_golden(golden, name, variant):
