@@ -328,7 +328,16 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  pdl_entry();  // before the first global read (num_tokens_post_padded)
+  // Programmatic dependent launch: the next kernel may be scheduled now.  A
+  // MoE GEMM waits for its predecessors here, before reading
+  // num_tokens_post_padded; a dense GEMM sets up first (barriers, TMEM) and
+  // its TMA weight producer never waits: the weights, shifts and tensor maps
+  // are not written by the kernels it may overlap (the weight repack is an
+  // ordinary launch, complete before any dependent starts), so its first
+  // weight stages stream while the predecessor finishes.  Every other thread
+  // waits before its first dependent access (activations, scales, outputs).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (p.moe) asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- the item space (identical in every thread; CTA pairs: in both CTAs) ----
   int n_blocks, n_items;
@@ -413,6 +422,7 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   if constexpr (kPair) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  if (!p.moe && warp != 0) asm volatile("griddepcontrol.wait;" ::: "memory");
   // barriers that pair traffic goes to: the leader's (rank 0) copy
   auto leader = [&](uint32_t bar) { return kPair ? mapa_shared(bar, 0) : bar; };
   // arrivals on the leader's barriers: CTA scope from the leader's own
