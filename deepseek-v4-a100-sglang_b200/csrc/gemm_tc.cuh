@@ -786,7 +786,9 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
       // the next 16 columns is issued before this chunk is processed, so its
       // latency overlaps the chunk's work.
       int32_t pre[16];
-      if constexpr (C::kIssuers == 1) tmem_ld_x16(t0 + 16 * eh, pre);
+      // stash tiles load the accumulator 32 columns at a time (their own loop)
+      constexpr bool kX32 = C::kStashCols > 0 && EPI != kEpiI32;
+      if constexpr (C::kIssuers == 1 && !kX32) tmem_ld_x16(t0 + 16 * eh, pre);
       bool acc_released = false;
       auto release_acc = [&]() {
         tc_fence_before();
@@ -975,30 +977,54 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
                       static_cast<int64_t>(orow) * p.ldo + n_g] = v[q];
           }
         }
-      } else if constexpr (C::kStashCols > 0) {
-        // phase 1: the whole accumulator -> scaled bf16 pairs in the stash
-        // (8 columns per 16-token chunk); the accumulator is handed back
-        // after the last chunk's load, so the next item's MMAs start now
+      } else if constexpr (kX32) {
+        // Stash tiles (256 tokens, one accumulator).  Phase 1: the whole
+        // accumulator -> scaled bf16 pairs in the TMEM stash (8 columns per
+        // 16-token chunk), 32 accumulator columns per load (group eh owns
+        // 32-column blocks eh, eh + EH, .. in both phases); the accumulator
+        // goes back after the warp's last load, so the next item's MMAs
+        // start while phase 2 transposes and stores from the stash.
         const uint32_t st0 = tmem + C::kStashBase + (static_cast<uint32_t>(quarter * 32) << 16);
-        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
-          int32_t v[16];
-          load16(c0, v);
-          uint32_t pk[8];
-          scale16(c0, v, pk);
-          tmem_st_x8(st0 + c0 / 2, pk);
+        for (int b0 = 32 * eh; b0 < n_mma; b0 += 32 * EH) {
+          int32_t w[32];
+          tmem_ld_x32_wait(t0 + b0, w);
+          if (b0 + 32 * EH >= n_mma) release_acc();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c0 = b0 + 16 * h;
+            if (c0 < n_mma) {
+              int32_t v[16];
+              if (kBiased) {
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                  const int4 r = reinterpret_cast<const int4*>(rs_s + c0)[q4];
+                  v[4 * q4] = r.x + w[16 * h + 4 * q4];
+                  v[4 * q4 + 1] = r.y + w[16 * h + 4 * q4 + 1];
+                  v[4 * q4 + 2] = r.z + w[16 * h + 4 * q4 + 2];
+                  v[4 * q4 + 3] = r.w + w[16 * h + 4 * q4 + 3];
+                }
+              } else {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) v[q] = w[16 * h + q];
+              }
+              uint32_t pk[8];
+              scale16(c0, v, pk);
+              tmem_st_x8(st0 + c0 / 2, pk);
+            }
+          }
         }
         tmem_st_wait();
-        // phase 2: transpose and store from the stash, the next chunk's
-        // stash load in flight during this chunk's work
-        uint32_t nx[8];
-        if (16 * eh < n_mma) tmem_ld_x8(st0 + 8 * eh, nx);
-        for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
-          tmem_ld_wait_regs8(nx);
-          uint32_t pk[8];
+        for (int b0 = 32 * eh; b0 < n_mma; b0 += 32 * EH) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) pk[q] = nx[q];
-          if (c0 + 16 * EH < n_mma) tmem_ld_x8(st0 + (c0 + 16 * EH) / 2, nx);
-          emit16(c0, pk);
+          for (int h = 0; h < 2; ++h) {
+            const int c0 = b0 + 16 * h;
+            if (c0 < n_mma) {
+              uint32_t pk[8];
+              tmem_ld_x8(st0 + c0 / 2, pk);
+              tmem_ld_wait_regs8(pk);
+              emit16(c0, pk);
+            }
+          }
         }
       } else {
         for (int c0 = 16 * eh; c0 < n_mma; c0 += 16 * EH) {
