@@ -56,6 +56,16 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def sustained_bf16():
+    """cuBLAS bf16 held for seconds under the power cap: the denominator for a
+    kernel timed inside a long loop (the prefill legs)."""
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 1400.0, "fallback"
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -771,14 +781,22 @@ def main():
             continue
         pre = legs[name]
         ops = pre["w13_ops"] + pre["w2_ops"]
+        sus_tf, sus_src = sustained_bf16()
+        tops_sus = 2.0 * sus_tf
+        achieved = ops / (pre["ms"] * 1e-3) / 1e12
         line[name] = {
             "workload": label,
             "value": PREFILL_M / (pre["ms"] * 1e-3), "unit": "tokens/s",
             "ms_per_step": pre["ms"], "block_m": pre["bm"], "experts_touched": pre["touched"],
-            "roofline": {"bound": "tensor", "achieved": ops / (pre["ms"] * 1e-3) / 1e12,
-                         "peak": tops_i8, "unit": "TOP/s (int8)",
-                         "frac": ops / (pre["ms"] * 1e-3) / 1e12 / tops_i8,
-                         "peak_source": f"2 x {peak_src} bf16 dense (kind::i8 rate = 2x kind::f16)",
+            # the prefill steps run inside a seconds-long loop under the power
+            # cap (clocks ~1.6-1.7 GHz): the sustained figure is the peak; the
+            # burst fraction is kept beside it
+            "roofline": {"bound": "tensor", "achieved": achieved,
+                         "peak": tops_sus, "unit": "TOP/s (int8)",
+                         "frac": achieved / tops_sus,
+                         "peak_source": f"2 x {sus_src} sustained bf16 dense (kind::i8 rate = "
+                                        "2x kind::f16; cuBLAS held for seconds under the power cap)",
+                         "frac_of_burst": achieved / tops_i8,
                          "w13_tops": pre["w13_ops"] / (pre["w13_ms"] * 1e-3) / 1e12,
                          "w2_tops": pre["w2_ops"] / (pre["w2_ms"] * 1e-3) / 1e12,
                          "w13_ms": pre["w13_ms"], "w2_ms": pre["w2_ms"]},
