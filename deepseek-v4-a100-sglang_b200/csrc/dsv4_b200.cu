@@ -321,6 +321,15 @@ int encode_act_map(TcGemmParams& p, const int8_t* a, int64_t rows, int64_t k, in
     cuuint32_t box[3] = {128, static_cast<cuuint32_t>(pair ? tn / 2 : tn), 2};
     r = encode_u8(&p.map_act, 3, a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    p.short_rows = 0;
+    if (r == CUDA_SUCCESS && !pair && tn > 64) {
+      // 64-row box of one 128-K half, for blocks with at most 64 tokens (MoE
+      // remainder blocks); a stage takes two, one into each half of its slot
+      cuuint32_t sbox[3] = {128, 64, 1};
+      r = encode_u8(&p.map_act_short, 3, a, dims, strides, sbox, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+      p.short_rows = 64;
+    }
   } else {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};

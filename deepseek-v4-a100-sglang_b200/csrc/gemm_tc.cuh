@@ -78,6 +78,10 @@ struct TcGemmParams {
   // activations int8 [a_rows][lda] as 2-D {K, a_rows}, box {128 B, 1 row},
   // 128-byte swizzle: rows are gathered 4 at a time (tile::gather4)
   CUtensorMap map_act;
+  // b_mode 2 on the sorted path: the same rows with a 64-row box, for blocks
+  // whose sorted position 64 is already padding (short_rows = 64; 0: unused)
+  CUtensorMap map_act_short;
+  int short_rows;
   int kb_per_expert;        // KB = K / 32
   int ss_per_expert;        // shift stride SS
   // activations
@@ -582,10 +586,23 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     if (tiled && warp == 3) {
       if (lane == 0) {
         tma_prefetch_desc(&p.map_act);
+        // A block whose sorted position short_rows holds padding has at most
+        // short_rows tokens (padding ends an expert's last block): its stages
+        // copy a short_rows-row box (the MMAs read only the block's columns).
+        // The test of the next item is read while the current one loads.
+        const bool use_short = !kPair && p.moe && p.b_mode == 2 && p.short_rows > 0;
+        if (use_short) tma_prefetch_desc(&p.map_act_short);
+        auto is_short = [&](int b) {
+          return __ldg(p.sorted_ids + static_cast<int64_t>(b) * p.block_m + p.short_rows) >=
+                 p.num_valid;
+        };
         uint32_t g = 0;
         ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
+        bool short_next = use_short && i_first < n_items ? is_short(walk.b) : false;
         for (int i = i_first; i < n_items; i += i_step) {
           const Item it = walk.get(i);
+          const bool shrt = short_next;
+          short_next = use_short && i + i_step < n_items ? is_short(walk.b) : false;
           if (!it.valid) continue;
           int ks0, nks;
           k_range(it, ks0, nks);
@@ -607,9 +624,18 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
               tma_load_3d_pair(b_base, &p.map_act, 0, row0 + pair_rank * C::kBRows,
                                (ks0 + s) * 2, rdy, pol);
             } else if (p.b_mode == 2) {
-              // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves
-              mbar_arrive_expect_tx(ready, static_cast<uint32_t>(C::kBBytes));
-              tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ready, pol);
+              // [K/128][rows][128]: one box {128, TN, 2} = both 128-K halves;
+              // short blocks: a {128, short_rows, 1} box into each half (the
+              // MMA descriptors address the second half kBHalf bytes on)
+              if (shrt) {
+                mbar_arrive_expect_tx(ready, static_cast<uint32_t>(p.short_rows) * 256u);
+                tma_load_3d(b_base, &p.map_act_short, 0, row0, (ks0 + s) * 2, ready, pol);
+                tma_load_3d(b_base + C::kBHalf, &p.map_act_short, 0, row0, (ks0 + s) * 2 + 1,
+                            ready, pol);
+              } else {
+                mbar_arrive_expect_tx(ready, static_cast<uint32_t>(C::kBBytes));
+                tma_load_3d(b_base, &p.map_act, 0, row0, (ks0 + s) * 2, ready, pol);
+              }
             } else {
               const int nhalf = stage_kb(ks0 + s) > 4 ? 2 : 1;
               mbar_arrive_expect_tx(ready, static_cast<uint32_t>(nhalf * C::kBHalf));
