@@ -1083,18 +1083,25 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
     const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t m1 = p.dec_m1, hi16 = p.dec_hi16, one = p.dec_one;
     uint32_t g = 0, cc = 0;
+    // MoE items all cover the whole K range, so their stage count is fixed
+    // and this group's first stage in the next item follows by a subtraction
+    // (the item start is a serial chain of control instructions on a busy
+    // sub-partition: every instruction taken out of it shortens the gap)
+    const int G = C::kDecodeGroups;
+    const int nks_moe = p.k_stages, nks_mod = p.k_stages % G;
+    int s_first = grp;  // g = 0
     ItemWalk walk(p, n_items, i_first, i_step, pair_rank);
     for (int i = i_first; i < n_items; i += i_step) {
       const Item it = walk.get(i);
       if (!it.valid) continue;
-      int ks0, nks;
-      k_range(it, ks0, nks);
+      int ks0 = 0, nks = nks_moe;
+      if (!p.moe) k_range(it, ks0, nks);
       // Only this group's stages are visited (s = s_first, s_first + G, ...):
       // stepping through the other groups' stages cost hundreds of cycles
       // each.  Every decode warp still takes part in every shift chunk (ring
       // discipline), whether or not it has a stage in it.
-      int s = static_cast<int>((grp - static_cast<int>(g % C::kDecodeGroups) + C::kDecodeGroups) %
-                               C::kDecodeGroups);
+      int s = p.moe ? s_first
+                    : static_cast<int>((grp - static_cast<int>(g % G) + G) % G);
       for (int c0 = 0; c0 < nks; c0 += C::kShChunk, ++cc) {
         mbar_wait(sh_full(cc % SHS), (cc / SHS) & 1, kErrWaitPackedFull);
         const uint8_t* SHC = smem + C::kOffSh + (cc % SHS) * C::kShSlotBytes;
@@ -1165,6 +1172,8 @@ mxfp4_int8_tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
         if (lane == 0) mbar_arrive(sh_empty(cc % SHS));
       }
       g += nks;
+      s_first -= nks_mod;
+      if (s_first < 0) s_first += G;
     }
   }
   tc_fence_before();
