@@ -40,7 +40,7 @@ EXP_RANGE = (-8, -4)
 # measured by an ncu capture of that kernel (dram__bytes_read.sum +
 # dram__bytes_write.sum); scales this launch's algorithmic bytes into the
 # roofline's `traffic`.
-TRAFFIC_RATIO_W13_DECODE = 1.015
+TRAFFIC_RATIO_W13_DECODE = 1.024
 
 
 def _set_experts(e):
