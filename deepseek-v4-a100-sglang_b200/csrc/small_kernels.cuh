@@ -93,8 +93,11 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ a
 // is written K-chunk-major, [K/128][cm_rows][128], the layout the GEMM's
 // sorted-row mode loads with one copy per stage, and rowsum[row] receives the
 // sum of the row's int8 values (for the GEMM's biased-unsigned decode).
+// Warp-per-row instances (K <= 2048: the sorted requant) are held to six
+// CTAs per SM: more resident warps outweigh the few spilled registers
+// (requant at M=8192 187 -> 172 us); the 128-thread rows keep the default.
 template <typename T, int RT, int VPT>
-__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict__ a, int64_t m,
+__global__ void __launch_bounds__(256, RT == 32 ? 6 : 0) quant_rows_reg_kernel(const T* __restrict__ a, int64_t m,
                                                              int64_t k, int64_t lda,
                                                              float clamp_abs,
                                                              int8_t* __restrict__ q,
