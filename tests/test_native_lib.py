@@ -75,3 +75,19 @@ def test_router_topk_argument_checks():
         D.router_topk(torch.zeros((4, 8), dtype=torch.int32), 2)
     with pytest.raises(RuntimeError, match="CUDA"):
         D.router_topk(torch.zeros((4, 8), dtype=torch.float32), 2)
+
+
+@pytest.mark.parametrize("compiler,std,ext", [("gcc", "-std=c99", "c"), ("g++", "-std=c++17", "cpp")])
+def test_header_compiles_standalone(tmp_path, compiler, std, ext):
+    """include/dsv4_b200.h is a plain C ABI: it compiles on its own as C99
+    and as C++17 with every warning an error (what a non-Python host sees)."""
+    import shutil
+    import subprocess
+    if shutil.which(compiler) is None:
+        pytest.skip(f"{compiler} not found")
+    src = tmp_path / f"use.{ext}"
+    src.write_text('#include "dsv4_b200.h"\nint main(void) { return DSV4_OK; }\n')
+    inc = Path(__file__).resolve().parent.parent / "include"
+    r = subprocess.run([compiler, std, "-Wall", "-Wextra", "-Werror", "-I", str(inc), "-c",
+                        str(src), "-o", str(tmp_path / "use.o")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
